@@ -1,0 +1,179 @@
+// C ABI entry points (include/sgld_b200.h): host-side argument checks, then one
+// asynchronous launch each.  No allocation, no synchronisation, no host readback.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "sgld_internal.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return SGLD_ERR_CUDA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int bit_length(int64_t x) {
+  int n = 0;
+  while (x > 0) {
+    ++n;
+    x >>= 1;
+  }
+  return n;
+}
+
+// Capacity contract of the reference's DecodeConfig (config.py:27-38), minus the
+// group-size whitelist (any integer group 1..16 is supported here).
+int check_geometry(const sgld_plan_geometry* g) {
+  if (g == nullptr) return fail(SGLD_ERR_INVALID_ARGUMENT, "geometry is NULL");
+  if (g->batch_capacity <= 0 || g->max_splits <= 0 || g->max_context <= 0 || g->groups <= 0 ||
+      g->workers <= 0)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "geometry fields must be positive");
+  const int64_t records = static_cast<int64_t>(g->batch_capacity) * g->max_splits;
+  if (records > sgld::kMaxRecords)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "record capacity batch_capacity*max_splits exceeds 4096");
+  if (records * g->groups >= (int64_t{1} << 31))
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "task capacity must stay below 2^31");
+  if (g->workers > sgld::kMaxPlanWorkers)
+    return fail(SGLD_ERR_UNSUPPORTED, "workers above 4096 are not supported");
+  return SGLD_OK;
+}
+
+int plan_buckets(const sgld_plan_geometry* g) {
+  const int64_t tiles = (static_cast<int64_t>(g->max_context) + sgld::kBlockKV - 1) / sgld::kBlockKV;
+  return bit_length(tiles - 1) + 1;
+}
+
+int check_plan_pointers(const sgld_plan_buffers* p) {
+  if (p == nullptr) return fail(SGLD_ERR_INVALID_ARGUMENT, "plan buffers are NULL");
+  const void* ptrs[] = {p->lengths, p->splits, p->active, p->counts, p->offsets, p->chunk,
+                        p->request, p->split, p->begin, p->end, p->weight, p->order,
+                        p->pack_first, p->pack_count, p->record_count, p->num_packs, p->mode,
+                        p->error, p->static_head, p->static_next};
+  for (const void* q : ptrs)
+    if (q == nullptr) return fail(SGLD_ERR_INVALID_ARGUMENT, "a plan buffer pointer is NULL");
+  return SGLD_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t sgld_abi_version(void) { return SGLD_ABI_VERSION; }
+
+const char* sgld_last_error(void) { return g_last_error.c_str(); }
+
+size_t sgld_layer_workspace_bytes(int32_t batch_capacity, int32_t query_heads, int32_t kv_heads,
+                                  int32_t head_dim, int32_t max_splits) {
+  if (batch_capacity <= 0 || query_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || max_splits <= 0)
+    return 0;
+  const size_t slots = static_cast<size_t>(batch_capacity) * query_heads * max_splits;
+  return 2 * sizeof(int32_t)                                   /* counter + exit ticket */
+         + slots * head_dim * sizeof(float)                    /* partial */
+         + slots * sizeof(float)                               /* lse */
+         + static_cast<size_t>(batch_capacity) * kv_heads * sizeof(int32_t) /* arrive */
+         + sizeof(int32_t);                                    /* status */
+}
+
+int sgld_plan_build(const sgld_plan_buffers* plan, const sgld_plan_geometry* geometry,
+                    int32_t force_mode, const int32_t* rules, int32_t n_rules,
+                    int32_t* layer_counters, int32_t n_counter_words, void* stream) {
+  int rc = check_geometry(geometry);
+  if (rc) return rc;
+  if ((rc = check_plan_pointers(plan))) return rc;
+  if (force_mode < -1 || force_mode > 4) return fail(SGLD_ERR_INVALID_ARGUMENT, "force_mode must be -1..4");
+  if (n_rules < 0 || (n_rules > 0 && rules == nullptr))
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "rules pointer/count mismatch");
+  if (n_counter_words < 0 || (n_counter_words > 0 && layer_counters == nullptr))
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "counter pointer/count mismatch");
+  sgld::PlanLaunch a;
+  a.p = *plan;
+  a.bcap = geometry->batch_capacity;
+  a.smax = geometry->max_splits;
+  a.maxctx = geometry->max_context;
+  a.groups = geometry->groups;
+  a.workers = geometry->workers;
+  a.buckets = plan_buckets(geometry);
+  a.force = force_mode;
+  a.rules = rules;
+  a.n_rules = n_rules;
+  a.counters = layer_counters;
+  a.n_counters = n_counter_words;
+  if (a.buckets > sgld::kMaxBuckets) return fail(SGLD_ERR_UNSUPPORTED, "max_context too large");
+  cudaError_t e = sgld::launch_plan(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sgld_plan_build launch");
+  return SGLD_OK;
+}
+
+int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers* plan,
+                           const sgld_plan_geometry* geometry, void* stream) {
+  if (args == nullptr) return fail(SGLD_ERR_INVALID_ARGUMENT, "decode args are NULL");
+  int rc = check_geometry(geometry);
+  if (rc) return rc;
+  if ((rc = check_plan_pointers(plan))) return rc;
+  const sgld_decode_args& d = *args;
+  if (!d.q || !d.k || !d.v || !d.out || !d.pages || !d.counter || !d.partial || !d.lse || !d.arrive ||
+      !d.status)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "a tensor or scratch pointer is NULL");
+  if (d.dtype != SGLD_DTYPE_F16 && d.dtype != SGLD_DTYPE_BF16)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "dtype must be fp16 or bf16");
+  if (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256)
+    return fail(SGLD_ERR_UNSUPPORTED, "supported head dimensions: 64, 128, 256");
+  if (d.kv_heads <= 0 || d.query_heads <= 0 || d.query_heads % d.kv_heads)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "query heads must be a positive multiple of KV heads");
+  const int group = d.query_heads / d.kv_heads;
+  if (group > 16) return fail(SGLD_ERR_UNSUPPORTED, "GQA group sizes above 16 are not supported");
+  if (d.kv_heads != geometry->groups)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "kv_heads must equal the plan's groups");
+  if (d.page_size <= 0) return fail(SGLD_ERR_INVALID_ARGUMENT, "page_size must be positive");
+  const bool csr = d.indptr != nullptr;
+  if (csr && d.page_size != 1) return fail(SGLD_ERR_INVALID_ARGUMENT, "CSR indexing uses page_size 1");
+  if (!(d.scale == d.scale)) return fail(SGLD_ERR_INVALID_ARGUMENT, "scale is NaN");
+
+  sgld::DecodeLaunch a;
+  a.d = d;
+  a.p = *plan;
+  a.bcap = geometry->batch_capacity;
+  a.smax = geometry->max_splits;
+  a.workers = geometry->workers;
+  a.group_size = group;
+  a.csr = csr ? 1 : 0;
+  if (csr) a.d.k_stride[1] = 0, a.d.v_stride[1] = 0;
+  bool fast_kv = aligned16(d.k) && aligned16(d.v) && d.k_stride[3] == 1 && d.v_stride[3] == 1;
+  for (int i = 0; i < 3; ++i) fast_kv = fast_kv && (a.d.k_stride[i] % 8 == 0) && (a.d.v_stride[i] % 8 == 0);
+  a.fast_kv = fast_kv ? 1 : 0;
+  a.fast_q = (aligned16(d.q) && d.q_stride[2] == 1 && d.q_stride[0] % 8 == 0 && d.q_stride[1] % 8 == 0) ? 1 : 0;
+  cudaError_t e = sgld::launch_decode(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent launch");
+  return SGLD_OK;
+}
+
+int sgld_merge_splits(const float* partial, const float* lse, const int32_t* counts,
+                      const int32_t* error, void* out, int32_t dtype, int32_t batch_capacity,
+                      int32_t query_heads, int32_t head_dim, int32_t max_splits, void* stream) {
+  if (!partial || !lse || !counts || !error || !out)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "a merge pointer is NULL");
+  if (dtype != SGLD_DTYPE_F16 && dtype != SGLD_DTYPE_BF16)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "dtype must be fp16 or bf16");
+  if (batch_capacity <= 0 || query_heads <= 0 || max_splits <= 0 || batch_capacity > 65535 ||
+      query_heads > 65535)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "merge geometry out of range");
+  if (head_dim <= 0 || head_dim > 1024) return fail(SGLD_ERR_UNSUPPORTED, "head_dim must be 1..1024");
+  cudaError_t e = sgld::launch_merge(partial, lse, counts, error, out, dtype, batch_capacity, query_heads,
+                                     head_dim, max_splits, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sgld_merge_splits launch");
+  return SGLD_OK;
+}
+
+}  // extern "C"

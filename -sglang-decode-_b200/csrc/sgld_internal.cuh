@@ -1,0 +1,45 @@
+// Internal declarations shared by the kernel translation units and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/sgld_b200.h"
+
+namespace sgld {
+
+constexpr int kBlockKV = 128;        // weight unit / tile of the reference (config.py:24)
+constexpr int kSplitAlign = 32;      // split chunk alignment (config.py:25)
+constexpr int kMaxRecords = 4096;    // record_capacity bound (config.py:37)
+constexpr int kMaxPlanWorkers = 4096;
+constexpr int kMaxBuckets = 32;
+
+struct PlanLaunch {
+  sgld_plan_buffers p;
+  int32_t bcap, smax, maxctx, groups, workers, buckets;
+  int32_t force;
+  const int32_t* rules;
+  int32_t n_rules;
+  int32_t* counters;
+  int32_t n_counters;
+};
+
+// Host-side launchers (return a cudaError_t of the launch).
+cudaError_t launch_plan(const PlanLaunch& a, cudaStream_t stream);
+
+struct DecodeLaunch {
+  sgld_decode_args d;
+  sgld_plan_buffers p;
+  int32_t bcap, smax, workers, group_size;
+  int32_t csr;
+  int32_t fast_kv;   // K/V rows are 16-byte aligned, unit stride along D
+  int32_t fast_q;    // Q rows are 16-byte aligned, unit stride along D
+};
+
+cudaError_t launch_decode(const DecodeLaunch& a, cudaStream_t stream);
+
+cudaError_t launch_merge(const float* partial, const float* lse, const int32_t* counts,
+                         const int32_t* error, void* out, int32_t dtype, int32_t bcap, int32_t hq,
+                         int32_t d, int32_t smax, cudaStream_t stream);
+
+}  // namespace sgld

@@ -1,0 +1,127 @@
+"""ctypes binding of the C-ABI kernel library ``libsgld_sm100.so`` (include/sgld_b200.h).
+
+This is the only path from Python to the GPU work of the decode hot path: there is
+no Triton, no torch fallback and no CPU fallback.  Importing is cheap; the library
+is loaded on first use and a missing or unloadable library raises immediately.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+from . import _build
+
+_I32P = ctypes.c_void_p
+
+
+class PlanGeometry(ctypes.Structure):
+    """sgld_plan_geometry."""
+    _fields_ = [("batch_capacity", ctypes.c_int32), ("max_splits", ctypes.c_int32),
+                ("max_context", ctypes.c_int32), ("groups", ctypes.c_int32),
+                ("workers", ctypes.c_int32)]
+
+
+PLAN_FIELDS = ("lengths", "splits", "active", "counts", "offsets", "chunk", "request", "split",
+               "begin", "end", "weight", "order", "pack_first", "pack_count", "record_count",
+               "num_packs", "mode", "error", "static_head", "static_next")
+
+
+class PlanBuffersC(ctypes.Structure):
+    """sgld_plan_buffers: device pointers of every plan array."""
+    _fields_ = [(name, ctypes.c_void_p) for name in PLAN_FIELDS]
+
+
+class DecodeArgs(ctypes.Structure):
+    """sgld_decode_args."""
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("out", ctypes.c_void_p), ("pages", ctypes.c_void_p), ("indptr", ctypes.c_void_p),
+        ("q_stride", ctypes.c_int64 * 3), ("k_stride", ctypes.c_int64 * 4),
+        ("v_stride", ctypes.c_int64 * 4), ("pt_stride", ctypes.c_int64 * 2),
+        ("dtype", ctypes.c_int32), ("query_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("page_size", ctypes.c_int32), ("scale", ctypes.c_float),
+        ("counter", ctypes.c_void_p), ("partial", ctypes.c_void_p), ("lse", ctypes.c_void_p),
+        ("arrive", ctypes.c_void_p), ("status", ctypes.c_void_p),
+    ]
+
+
+DTYPE_F16, DTYPE_BF16 = 0, 1
+STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error"}
+EXPORTS = ("sgld_abi_version", "sgld_last_error", "sgld_layer_workspace_bytes", "sgld_plan_build",
+           "sgld_decode_persistent", "sgld_merge_splits")
+ABI_VERSION = 1
+
+_lock = threading.Lock()
+_lib = None
+
+
+class NativeError(RuntimeError):
+    """A C-ABI call returned a non-zero sgld_status."""
+
+
+def load(path=None):
+    """Load (once) and return the ctypes handle; raise if the library is unavailable."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        lib_path = path or _build.library_path()
+        if not lib_path.exists():
+            raise RuntimeError(
+                f"{lib_path} is missing: build the CUDA extension first "
+                "(python -m sglang_decode._build or __graft_entry__.build()); "
+                "there is no fallback implementation")
+        lib = ctypes.CDLL(str(lib_path))
+        lib.sgld_abi_version.restype = ctypes.c_int32
+        lib.sgld_last_error.restype = ctypes.c_char_p
+        lib.sgld_layer_workspace_bytes.restype = ctypes.c_size_t
+        lib.sgld_layer_workspace_bytes.argtypes = [ctypes.c_int32] * 5
+        lib.sgld_plan_build.restype = ctypes.c_int
+        lib.sgld_plan_build.argtypes = [ctypes.POINTER(PlanBuffersC), ctypes.POINTER(PlanGeometry),
+                                        ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32,
+                                        ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
+        lib.sgld_decode_persistent.restype = ctypes.c_int
+        lib.sgld_decode_persistent.argtypes = [ctypes.POINTER(DecodeArgs), ctypes.POINTER(PlanBuffersC),
+                                               ctypes.POINTER(PlanGeometry), ctypes.c_void_p]
+        lib.sgld_merge_splits.restype = ctypes.c_int
+        lib.sgld_merge_splits.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int32] * 5 + [ctypes.c_void_p]
+        if lib.sgld_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"{lib_path}: ABI version {lib.sgld_abi_version()} != {ABI_VERSION}")
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().sgld_last_error().decode(errors="replace")
+        kind = STATUS.get(rc, str(rc))
+        if rc in (1, 2):
+            raise ValueError(f"{what}: {kind}: {msg}")
+        raise NativeError(f"{what}: {kind}: {msg}")
+
+
+def layer_workspace_bytes(batch_capacity, query_heads, kv_heads, head_dim, max_splits) -> int:
+    return int(load().sgld_layer_workspace_bytes(batch_capacity, query_heads, kv_heads, head_dim,
+                                                 max_splits))
+
+
+def plan_build(plan_c, geometry_c, force_mode, rules_ptr, n_rules, counters_ptr, n_counters, stream):
+    rc = load().sgld_plan_build(ctypes.byref(plan_c), ctypes.byref(geometry_c), int(force_mode),
+                                rules_ptr, int(n_rules), counters_ptr, int(n_counters), stream)
+    check(rc, "sgld_plan_build")
+
+
+def decode_persistent(args_c, plan_c, geometry_c, stream):
+    rc = load().sgld_decode_persistent(ctypes.byref(args_c), ctypes.byref(plan_c),
+                                       ctypes.byref(geometry_c), stream)
+    check(rc, "sgld_decode_persistent")
+
+
+def merge_splits(partial, lse, counts, error, out, dtype, batch_capacity, query_heads, head_dim,
+                 max_splits, stream):
+    rc = load().sgld_merge_splits(partial, lse, counts, error, out, dtype, batch_capacity,
+                                  query_heads, head_dim, max_splits, stream)
+    check(rc, "sgld_merge_splits")

@@ -1,0 +1,119 @@
+"""Plan/execute API shared by the standalone harness and the SGLang adapter.
+
+Same API and checks as the reference's ``runtime/engine.py:1-74``:
+``DecodeEngine(config, device, dtype, layers, rules, force_mode)`` with
+``prepare()`` (GPU plan build, once per compatible group per step) and
+``execute(q, k, v, pages, layer=0, *, indptr=None, scale=None)`` (paged
+``[page, token, head, dim]`` or CSR ``[token, head, dim]`` KV, arbitrary strides).
+``execute`` is ONE launch of the sm_100a persistent decode kernel with the split
+merge fused in; the claim counter is reset by the plan build and left at zero by
+the decode launch itself (the reference's per-layer memset is not needed).
+"""
+from dataclasses import dataclass
+
+import torch
+
+from .. import _native
+from ..config import DecodeConfig
+from ..planning.builder import build_plan
+from .workspace import LayerBuffers, PlanBuffers
+
+_DTYPES = {torch.float16: _native.DTYPE_F16, torch.bfloat16: _native.DTYPE_BF16}
+
+
+@dataclass(frozen=True)
+class PlanKey:
+    """Caller-supplied sequence identity; pointer equality alone is insufficient."""
+    sequence_layout: str
+    split_layout: str
+    head_layout: tuple
+    attention_window: str = "full"
+
+
+class DecodeEngine:
+    def __init__(self, config: DecodeConfig, device="cuda", dtype=torch.bfloat16,
+                 layers=1, rules=(), force_mode=-1):
+        self.config, self.force_mode = config, force_mode
+        self.dtype = dtype
+        self.plan = PlanBuffers(config, device, rules)
+        self.plan.has_static_rule = any(r.mode == 2 for r in rules)
+        # One contiguous array of per-layer claim counters, reset by every plan build.
+        self.counters = torch.zeros((layers, 2), dtype=torch.int32, device=self.plan.device)
+        self.plan.register_counters(self.counters)
+        self.layers = [LayerBuffers.allocate(config, self.plan.device, dtype, counter=self.counters[i])
+                       for i in range(layers)]
+
+    def prepare(self):
+        """Call once per compatible group per step, including on every graph replay."""
+        build_plan(self.plan, self.force_mode)
+
+    def execute(self, q, k, v, pages, layer=0, *, indptr=None, scale=None):
+        """KV layout: [pages,page_size,kv_heads,D], or CSR [tokens,kv_heads,D].
+
+        Metadata and Q/KV must be ready on the current CUDA stream. Fixed buffers
+        are reused; consumers must finish before reusing this execution instance.
+        """
+        c, p, out = self.config, self.plan, self.layers[layer]
+        if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+            raise ValueError("BF16/FP16 Q/K/V of identical dtype are required")
+        if tuple(q.shape) != (c.batch_capacity, c.query_heads, c.head_dim):
+            raise ValueError("Q must use the capture capacity; pad inactive rows")
+        if out.output.dtype != q.dtype:
+            raise ValueError("Q dtype differs from the engine's output dtype")
+        for t in (q, k, v, pages):
+            if t.device != p.device:
+                raise ValueError("all tensors must live on the engine's device")
+        if pages.dtype != torch.int32:
+            raise ValueError("page table / kv_indices must be int32")
+        a = out.c_args
+        if indptr is None:
+            if k.ndim != 4 or v.ndim != 4 or k.shape != v.shape:
+                raise ValueError("paged KV must have matching [page,token,head,dim] shapes")
+            if tuple(k.shape[1:]) != (c.page_size, c.kv_heads, c.head_dim):
+                raise ValueError("KV geometry differs from the capture configuration")
+            if tuple(pages.shape) != (c.batch_capacity, c.max_pages):
+                raise ValueError("page table capacity mismatch")
+            a.k_stride[:] = k.stride()
+            a.v_stride[:] = v.stride()
+            a.pt_stride[:] = pages.stride()
+            a.indptr = None
+            a.page_size = c.page_size
+        else:
+            if k.ndim != 3 or v.shape != k.shape or tuple(k.shape[1:]) != (c.kv_heads, c.head_dim):
+                raise ValueError("CSR KV must be [token,head,dim]")
+            if c.page_size != 1 or pages.ndim != 1:
+                raise ValueError("CSR integration uses one-token physical pages")
+            if indptr.dtype != torch.int32 or indptr.ndim != 1:
+                raise ValueError("kv_indptr must be a 1-D int32 tensor")
+            ks, vs = k.stride(), v.stride()
+            a.k_stride[:] = (ks[0], 0, ks[1], ks[2])
+            a.v_stride[:] = (vs[0], 0, vs[1], vs[2])
+            a.pt_stride[:] = (0, 0)
+            a.indptr = indptr.data_ptr()
+            a.page_size = 1
+        a.q, a.k, a.v, a.out, a.pages = (q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                         out.output.data_ptr(), pages.data_ptr())
+        a.q_stride[:] = q.stride()
+        a.dtype = _DTYPES[q.dtype]
+        a.query_heads, a.kv_heads, a.head_dim = c.query_heads, c.kv_heads, c.head_dim
+        a.scale = c.head_dim ** -0.5 if scale is None else float(scale)
+        a.counter, a.partial, a.lse = out.counter.data_ptr(), out.partial.data_ptr(), out.lse.data_ptr()
+        a.arrive, a.status = out.arrive.data_ptr(), out.status.data_ptr()
+        stream = torch.cuda.current_stream(p.device).cuda_stream
+        _native.decode_persistent(a, p.c_buffers, p.c_geometry, stream)
+        return out.output
+
+
+def merge_splits(partial, lse, counts, error, out):
+    """Stand-alone split merge (reference kernels/merge.py:7-30) into ``out`` [B, Hq, D]."""
+    if partial.dtype != torch.float32 or lse.dtype != torch.float32:
+        raise ValueError("partial and lse must be fp32")
+    if out.dtype not in _DTYPES or not out.is_contiguous() or not partial.is_contiguous():
+        raise ValueError("out must be contiguous fp16/bf16 and partial contiguous")
+    b, hq, smax, d = partial.shape
+    if tuple(lse.shape) != (b, hq, smax) or tuple(out.shape) != (b, hq, d) or counts.numel() < b:
+        raise ValueError("merge shapes disagree")
+    stream = torch.cuda.current_stream(partial.device).cuda_stream
+    _native.merge_splits(partial.data_ptr(), lse.data_ptr(), counts.data_ptr(), error.data_ptr(),
+                         out.data_ptr(), _DTYPES[out.dtype], b, hq, d, smax, stream)
+    return out

@@ -1,0 +1,394 @@
+#!/usr/bin/env python3
+"""Benchmark: paged GQA decode µs/layer + achieved HBM TB/s on 1/2/4/8 B200.
+
+One step = one decode layer over the workload's whole batch: the GPU plan build
+(``DecodeEngine.prepare``) plus the fused persistent decode + split merge
+(``DecodeEngine.execute``), the same time boundary as the reference's
+``benchmarks/bench_decode.py:94`` (plan begin through reset/attention/merge).
+
+Default workload: C3 (Llama-3-70B shape, B=256, Hq=64, Hkv=8, D=128, fp16, CSR,
+L~U[1024,8192]) -- the configuration whose KV heads shard over 1/2/4/8 GPUs.  Under
+``torchrun`` each rank owns Hkv/N KV heads (and Hq/N query heads) and its slice of
+the KV pool; there is no collective on the timed path (strong scaling: total work
+fixed).  ``value`` = µs per layer for the whole job = max over ranks.
+
+Also reported: ``roofline`` of the decode kernel (algorithmic bytes / CUDA-event
+time of its launches, vs the measured HBM copy peak), ``e2e`` (the same step through
+the public API with per-step host->device copies of the step's inputs from pinned
+memory and a device->host copy of the output), ``cpu_baseline`` (the FP32 CPU oracle
+on a bounded sample, scaled to one layer) and SM clocks sampled during the timed
+region.  ``--impl reference`` times the reference's CPU implementation (the oracle
+restatement) instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "-sglang-decode-_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "paged GQA decode µs/layer + achieved HBM TB/s vs peak at 1/2/4/8 B200"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="C3", choices=["C1", "C2", "C3", "C4"])
+    ap.add_argument("--mode", type=int, default=-1, help="-1 AUTO, 0..4 force a mode")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- helpers
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            data = json.loads(path.read_text())
+            return float(data["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu_index)],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.file.flush()
+
+    def summary(self):
+        rows = []
+        try:
+            with open(self.file.name) as f:
+                for line in f:
+                    parts = [x.strip() for x in line.split(",")]
+                    if len(parts) >= 9:
+                        rows.append(parts)
+        finally:
+            os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        power = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(power) if power else None}
+
+
+def algorithmic_bytes(b, kv_heads_local, q_heads_local):
+    """Σ L·Hkv·D·2(K,V)·elem + Q + O + index bytes (4·ΣL CSR, 4·Σceil(L/ps) paged)."""
+    import torch
+    elem = torch.finfo(b.dtype).bits // 8
+    c = b.config
+    total = sum(b.lengths)
+    kv = total * kv_heads_local * c.head_dim * 2 * elem
+    qo = 2 * len(b.lengths) * q_heads_local * c.head_dim * elem
+    idx = 4 * total if b.csr else 4 * sum(math.ceil(n / c.page_size) for n in b.lengths)
+    return kv + qo + idx
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_reference_sample(b, target_seconds, max_rounds=None):
+    """Time the FP32 CPU oracle on a seeded sample of the workload's requests.
+
+    Requests are processed in parallel, one per host thread (BLAS limited to one
+    thread per worker), in rounds of ``threads`` requests, until ``target_seconds``
+    of wall time or ``max_rounds`` rounds.  K/V rows come from a seeded fp16 pool of
+    up to 65536 tokens (same shapes, N(0,1) values); each request gathers its own
+    random rows.  Returns (µs per layer scaled by tokens, sample text, threads).
+    """
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+
+    from oracle import attention as A
+    c = b.config
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(17)
+    rows = min(sum(b.lengths), 1 << 16)
+    k = rng.standard_normal((rows, c.kv_heads, c.head_dim), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((rows, c.kv_heads, c.head_dim), dtype=np.float32).astype(np.float16)
+    q = rng.standard_normal((1, c.query_heads, c.head_dim), dtype=np.float32).astype(np.float16)
+    requests = [n for n in b.lengths if n > 0]
+    index_sets = [rng.integers(0, rows, n).astype(np.int32) for n in requests[:threads * 64]]
+
+    def one(i):
+        n = requests[i % len(requests)]
+        idx = index_sets[i % len(index_sets)]
+        return A.csr_attention(q, k, v, np.array([0, n]), idx, [n])
+
+    done_tokens, elapsed, rounds, i = 0, 0.0, 0, 0
+    with threadpool_limits(1), ThreadPoolExecutor(threads) as pool:
+        while (max_rounds is None or rounds < max_rounds) and (elapsed < target_seconds or rounds == 0):
+            batch = list(range(i, i + threads))
+            t0 = time.perf_counter()
+            list(pool.map(one, batch))
+            elapsed += time.perf_counter() - t0
+            done_tokens += sum(requests[j % len(requests)] for j in batch)
+            i += threads
+            rounds += 1
+    total_tokens = sum(b.lengths)
+    per_layer_us = elapsed / max(done_tokens, 1) * total_tokens * 1e6
+    sample = (f"{i} requests ({done_tokens} tokens of a {total_tokens}-token layer) in {rounds} "
+              f"parallel rounds, scaled by tokens")
+    return per_layer_us, sample, threads
+
+
+def _cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        counts = [p.get("num_threads", 1) for p in threadpool_info() if p.get("user_api") == "blas"]
+        if counts:
+            return int(max(counts))
+    except Exception:  # noqa: BLE001 -- reporting only
+        pass
+    return os.cpu_count() or 1
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (FP32 oracle restatement), rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from sglang_decode.workloads import baseline
+    b = baseline(args.workload)
+    # One step = one bounded sample: one parallel round of requests on all host threads.
+    steps = []
+    for i in range(args.warmup + args.steps):
+        us, sample, threads = cpu_reference_sample(b, 0.0, max_rounds=1)
+        if i >= args.warmup:
+            steps.append(us)
+    value = statistics.median(steps)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "us/layer",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(value / 1000, 3), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload} (reference FP32 CPU path, scaled per layer)"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "us/layer", "cores": threads,
+                         "kind": "port", "sample": "per step: " + sample},
+        "e2e": {"value": round(value, 2), "unit": "us/layer", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from sglang_decode.config import DecodeConfig
+    from sglang_decode.runtime.engine import DecodeEngine
+    from sglang_decode.workloads import baseline, generate, update_plan
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    b = baseline(args.workload, workers=sms)
+    c = b.config
+    if c.kv_heads % world:
+        raise SystemExit(f"{c.kv_heads} KV heads do not shard over {world} GPUs")
+    hkv = c.kv_heads // world
+    hq = c.query_heads // world
+    cfg = DecodeConfig(batch_capacity=c.batch_capacity, max_splits=c.max_splits,
+                       max_context=c.max_context, query_heads=hq, kv_heads=hkv,
+                       head_dim=c.head_dim, page_size=c.page_size, workers=sms)
+    data = generate(b, device=device, seed=17, kv_heads=hkv, head_offset=rank * hkv)
+    engine = DecodeEngine(cfg, device=device, dtype=b.dtype, force_mode=args.mode)
+    update_plan(engine, b.lengths, b.splits)
+    q, k, v, pages, indptr = data["q"], data["k"], data["v"], data["pages"], data["indptr"]
+
+    def step():
+        engine.prepare()
+        return engine.execute(q, k, v, pages, indptr=indptr)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    out_check = step().clone()
+    torch.cuda.synchronize()
+    if engine.layers[0].status.item() != 0 or not torch.isfinite(out_check[:len(b.lengths)].float()).all():
+        raise SystemExit("decode self-check failed (status word or non-finite output)")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-timed region (inputs resident in HBM; KV pool >> L2, no flush needed)
+    stream = torch.cuda.current_stream(device)
+    dec_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(args.steps):
+            engine.prepare()
+            dec_events[i][0].record(stream)
+            engine.execute(q, k, v, pages, indptr=indptr)
+            dec_events[i][1].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    total_ms = start.elapsed_time(end)
+    dec_ms = statistics.mean(s.elapsed_time(e) for s, e in dec_events)
+
+    # ---- end to end through the public API, host buffers, copies inside the region
+    e2e_steps = args.e2e_steps or max(10, args.steps // 4)
+    pin = lambda t: t.detach().to("cpu").pin_memory()
+    h_q = pin(q)
+    h_pages = pin(pages)
+    h_indptr = pin(indptr) if indptr is not None else None
+    h_meta = torch.tensor([b.lengths + [0] * (c.batch_capacity - len(b.lengths)),
+                           b.splits + [1] * (c.batch_capacity - len(b.lengths))],
+                          dtype=torch.int32).pin_memory()
+    h_out = torch.empty(engine.layers[0].output.shape, dtype=b.dtype).pin_memory()
+    d_q, d_pages = torch.empty_like(q), torch.empty_like(pages)
+    d_indptr = torch.empty_like(indptr) if indptr is not None else None
+    d_meta = torch.empty((2, c.batch_capacity), dtype=torch.int32, device=device)
+    h2d = h_q.numel() * h_q.element_size() + h_pages.numel() * 4 + h_meta.numel() * 4 + (
+        h_indptr.numel() * 4 if h_indptr is not None else 0)
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        d_q.copy_(h_q, non_blocking=True)
+        d_pages.copy_(h_pages, non_blocking=True)
+        d_meta.copy_(h_meta, non_blocking=True)
+        if d_indptr is not None:
+            d_indptr.copy_(h_indptr, non_blocking=True)
+        engine.plan.lengths.copy_(d_meta[0])
+        engine.plan.splits.copy_(d_meta[1])
+        engine.prepare()
+        out = engine.execute(d_q, k, v, d_pages, indptr=d_indptr)
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if not torch.equal(h_out[:len(b.lengths)], out_check[:len(b.lengths)].cpu()):
+        raise SystemExit("e2e output differs from the device-resident run")
+
+    # ---- max over ranks
+    step_ms = total_ms / args.steps
+    stats = torch.tensor([step_ms, dec_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    step_ms, dec_ms, e2e_ms = stats.tolist()
+    bytes_launch = algorithmic_bytes(b, hkv, hq)
+    achieved = bytes_launch / (dec_ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    clock = clocks.summary()
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            us, sample, threads = cpu_reference_sample(b, args.cpu_sample_seconds)
+            cpu = {"value": round(us, 1), "unit": "us/layer", "cores": threads, "kind": "port",
+                   "sample": sample}
+        line = {
+            "metric": METRIC, "value": round(step_ms * 1000, 2), "unit": "us/layer",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(step_ms, 4), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": {torch.float16: "f16", torch.bfloat16: "bf16"}[b.dtype],
+            "data": "synthetic",
+            "config": {"workload": f"{b.name}: B={len(b.lengths)} Hq={c.query_heads} Hkv={c.kv_heads} "
+                                   f"D={c.head_dim} {'CSR' if b.csr else f'paged ps={c.page_size}'} "
+                                   f"sum(L)={sum(b.lengths)}",
+                       "mode": "AUTO" if args.mode < 0 else args.mode,
+                       "heads_per_gpu": {"kv": hkv, "q": hq}, "workers": sms,
+                       "l2": "not flushed: KV pool per GPU > 126 MB L2"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": peak_kind, "kernel": "sgld decode_kernel (fused decode+merge)",
+                         "bytes_per_launch": bytes_launch, "kernel_us": round(dec_ms * 1000, 2)},
+            "e2e": {"value": round(e2e_ms * 1000, 2), "unit": "us/layer", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clock,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
