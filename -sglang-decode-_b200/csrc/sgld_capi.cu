@@ -1,9 +1,13 @@
 // C ABI entry points (include/sgld_b200.h): host-side argument checks, then one
 // asynchronous launch each.  No allocation, no synchronisation, no host readback.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "sgld_internal.cuh"
@@ -55,6 +59,49 @@ int plan_buckets(const sgld_plan_geometry* g) {
   return bit_length(tiles - 1) + 1;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 4D map {D, Hkv, page_size, pages} over a paged K or V tensor with element strides
+// (head, token-in-page, page); boxes of {64 dims, 1 head, box_rows tokens, 1 page}
+// land in shared memory with the 128-byte swizzle.
+bool encode_paged_map(CUtensorMap* map, const void* base, int32_t dtype, int64_t d, int64_t hkv, int64_t ps,
+                      int64_t pages, const int64_t* stride, int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(hkv), static_cast<cuuint64_t>(ps),
+                        static_cast<cuuint64_t>(pages)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(stride[2]) * 2, static_cast<cuuint64_t>(stride[1]) * 2,
+                           static_cast<cuuint64_t>(stride[0]) * 2};
+  for (cuuint64_t st : strides)
+    if (st == 0 || st % 16 != 0 || st >= (cuuint64_t{1} << 40)) return false;
+  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType type =
+      dtype == SGLD_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, type, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool tma_disabled_by_env() {
+  const char* v = std::getenv("SGLD_DISABLE_TMA");
+  return v != nullptr && v[0] == '1';
+}
+
 int check_plan_pointers(const sgld_plan_buffers* p) {
   if (p == nullptr) return fail(SGLD_ERR_INVALID_ARGUMENT, "plan buffers are NULL");
   const void* ptrs[] = {p->lengths, p->splits, p->active, p->counts, p->offsets, p->chunk,
@@ -82,7 +129,6 @@ size_t sgld_layer_workspace_bytes(int32_t batch_capacity, int32_t query_heads, i
   return 2 * sizeof(int32_t)                                   /* counter + exit ticket */
          + slots * head_dim * sizeof(float)                    /* partial */
          + slots * sizeof(float)                               /* lse */
-         + static_cast<size_t>(batch_capacity) * kv_heads * sizeof(int32_t) /* arrive */
          + sizeof(int32_t);                                    /* status */
 }
 
@@ -123,8 +169,7 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   if (rc) return rc;
   if ((rc = check_plan_pointers(plan))) return rc;
   const sgld_decode_args& d = *args;
-  if (!d.q || !d.k || !d.v || !d.out || !d.pages || !d.counter || !d.partial || !d.lse || !d.arrive ||
-      !d.status)
+  if (!d.q || !d.k || !d.v || !d.out || !d.pages || !d.counter || !d.partial || !d.lse || !d.status)
     return fail(SGLD_ERR_INVALID_ARGUMENT, "a tensor or scratch pointer is NULL");
   if (d.dtype != SGLD_DTYPE_F16 && d.dtype != SGLD_DTYPE_BF16)
     return fail(SGLD_ERR_INVALID_ARGUMENT, "dtype must be fp16 or bf16");
@@ -142,6 +187,7 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   if (!(d.scale == d.scale)) return fail(SGLD_ERR_INVALID_ARGUMENT, "scale is NaN");
 
   sgld::DecodeLaunch a;
+  std::memset(&a, 0, sizeof(a));
   a.d = d;
   a.p = *plan;
   a.bcap = geometry->batch_capacity;
@@ -154,8 +200,25 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   for (int i = 0; i < 3; ++i) fast_kv = fast_kv && (a.d.k_stride[i] % 8 == 0) && (a.d.v_stride[i] % 8 == 0);
   a.fast_kv = fast_kv ? 1 : 0;
   a.fast_q = (aligned16(d.q) && d.q_stride[2] == 1 && d.q_stride[0] % 8 == 0 && d.q_stride[1] % 8 == 0) ? 1 : 0;
-  cudaError_t e = sgld::launch_decode(a, static_cast<cudaStream_t>(stream));
+  // Paged KV by tensor-map TMA: a box of 32 tokens never crosses a page because stages
+  // start 32-token aligned and 32 divides the page size.  Smaller pages stay on the
+  // multi-warp cp.async path, which measured faster than 8- or 16-row boxes.
+  const int ps = d.page_size;
+  if (!csr && fast_kv && ps % 32 == 0 && d.kv_extent > 0 &&
+      d.kv_extent < (int64_t{1} << 31) && !tma_disabled_by_env()) {
+    const int box_rows = 32;
+    if (encode_paged_map(&a.kmap, d.k, d.dtype, d.head_dim, d.kv_heads, ps, d.kv_extent, d.k_stride, box_rows) &&
+        encode_paged_map(&a.vmap, d.v, d.dtype, d.head_dim, d.kv_heads, ps, d.kv_extent, d.v_stride, box_rows)) {
+      a.tma_kv = 1;
+      a.box_rows = box_rows;
+    }
+  }
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = sgld::launch_decode(a, st);
   if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent launch");
+  e = sgld::launch_merge(d.partial, d.lse, plan->counts, plan->error, d.out, d.dtype, geometry->batch_capacity,
+                         d.query_heads, d.head_dim, geometry->max_splits, st, true);
+  if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent merge launch");
   return SGLD_OK;
 }
 
@@ -169,9 +232,11 @@ int sgld_merge_splits(const float* partial, const float* lse, const int32_t* cou
   if (batch_capacity <= 0 || query_heads <= 0 || max_splits <= 0 || batch_capacity > 65535 ||
       query_heads > 65535)
     return fail(SGLD_ERR_INVALID_ARGUMENT, "merge geometry out of range");
-  if (head_dim <= 0 || head_dim > 1024) return fail(SGLD_ERR_UNSUPPORTED, "head_dim must be 1..1024");
+  if (head_dim <= 0 || head_dim % 4 != 0 || head_dim > 4096)
+    return fail(SGLD_ERR_UNSUPPORTED, "head_dim must be a multiple of 4 up to 4096");
+  if (!aligned16(partial)) return fail(SGLD_ERR_INVALID_ARGUMENT, "partial must be 16-byte aligned");
   cudaError_t e = sgld::launch_merge(partial, lse, counts, error, out, dtype, batch_capacity, query_heads,
-                                     head_dim, max_splits, static_cast<cudaStream_t>(stream));
+                                     head_dim, max_splits, static_cast<cudaStream_t>(stream), false);
   if (e != cudaSuccess) return cuda_fail(e, "sgld_merge_splits launch");
   return SGLD_OK;
 }

@@ -1,38 +1,40 @@
-// Persistent paged GQA decode for sm_100a with the split merge fused in.
+// Persistent paged GQA decode for sm_100a.
 //
 // Replaces the reference's persistent_decode + _attention_task
-// (kernels/attention.py:12-130) and merge_splits (kernels/merge.py:7-30), and the
-// per-layer counter memset (runtime/engine.py:62).
+// (kernels/attention.py:12-130) and the per-layer counter memset
+// (runtime/engine.py:62).  The split merge (merge.py) is the next launch
+// (sgld_merge.cu), chained to this one by programmatic dependent launch.
 //
-// One CTA per worker (grid = workers), six warps with fixed roles:
+// One CTA per worker (grid = workers).  Warps have fixed roles and are connected by
+// shared-memory rings guarded by mbarriers:
 //
-//   warp 5  scheduler  claims tasks exactly as the reference's claim loop
-//                      (attention.py:99-130: R0/R1 stride-W round robin, STATIC list
-//                      walk, D1/D4 relaxed atomic per pack), resolves each task to
-//                      (request, split, kv_head, token range) (attention.py:23-47)
-//                      and pushes it into a 4-deep shared-memory task queue.
-//   warp 4  producer   streams each task's K/V rows, 64 tokens per stage, into a
-//                      multi-stage shared-memory ring with 16-byte cp.async
-//                      (page-table or CSR gather, arbitrary 16B-aligned strides),
-//                      completion tracked by mbarriers; loads the task's query
-//                      group into a double-buffered Q slot.  Indices for the next
-//                      stage are prefetched while the current one is issued.
-//   warps 0-3 consumers each take 16 tokens of a stage.  QK and PV run on tensor
-//                      cores (mma.sync m16n8k16) in "swapped" form so the GQA group
-//                      (padded to 8 or 16) is the N dimension: S^T = K Q^T and
-//                      O^T += V^T P^T; movmatrix turns the score accumulator into
-//                      the P^T operand.  FP32 online softmax state is warp-private;
-//                      at the end of a task the four warp states are combined.
+//   scheduler (1 warp, lane 0)  claims tasks exactly as the reference's claim loop
+//        (attention.py:99-130: R0/R1 stride-W round robin, STATIC list walk, D1/D4
+//        relaxed atomic per pack), resolves each task to (request, split, kv_head,
+//        token range) (attention.py:23-47) and pushes it into the task ring.
+//   indexer (1 warp)  turns tasks into 64-token stage descriptors: it gathers the
+//        page-table / CSR indices of four stages per round trip, with the next batch's
+//        loads in flight while the current batch is written, and stores each token's
+//        page, in-page row and K/V row offsets (any strides) in the descriptor ring.
+//   producers (P warps)  fill the data ring.  Paged KV with a page_size that is a
+//        multiple of 32 moves by tensor-map TMA boxes (64 dims x 32 tokens of one page
+//        per instruction); CSR and other layouts move by 16-byte cp.async spread over
+//        the P warps (the issue rate of one warp caps its bandwidth).
+//        Producer 0 also loads each task's query group into a double-buffered Q slot.
+//   consumers (4 warps)  each take 16 tokens of a stage.  QK and PV run on tensor
+//        cores (mma.sync m16n8k16) in "swapped" form so the GQA group (padded to 8 or
+//        16) is the N dimension: S^T = K Q^T and O^T += V^T P^T; movmatrix turns the
+//        score accumulator into the P^T operand.  FP32 online softmax state is
+//        warp-private; at the end of a task the four warp states are combined and
+//        the normalised partial and natural-log LSE of every query head of the group
+//        are stored to slot (request*Hq + head)*Smax + split (attention.py:81-84).
 //
-// Every task writes its normalised partial and natural-log LSE to slot
-// (request*Hq + head)*Smax + split (attention.py:81-84).  The CTA whose split is the
-// last to arrive for (request, kv_head) merges all splits in split order
-// (merge.py:17-27) and writes the output; single-split requests write the output
-// directly (the merge of one split is the identity).  Rows without records are
-// written as zeros, or NaN when the plan's error word is set (merge.py:28-30).
-//
-// Every mbarrier wait is bounded; on expiry a status bit is set and the CTA
-// unwinds.  The claim counter and the arrival counters are left at zero.
+// Shared-memory tiles use the 128-byte swizzle layout [D/64][rows][128 B] (16-byte
+// chunk index XOR row%8) that TMA writes natively; ldmatrix reads are bank-conflict
+// free.  Rows past a task's last token are masked in registers (scores -inf, V
+// fragments zero), so stale shared memory never reaches the result.  Every mbarrier
+// wait is bounded; on expiry a status bit is set and the warp unwinds.  The claim
+// counter is left at zero.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -44,16 +46,16 @@ namespace sgld {
 namespace {
 
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s per wait
-constexpr int kSmemBudget = 227 * 1024;
+constexpr int kSmemBudget = 227 * 1024 - 1024;     // 1 KB slack to align the base to 1024
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 enum : int { kFlagFirst = 1, kFlagLast = 2, kFlagExit = 4 };
 enum : int { kStatusWaitFull = 1, kStatusWaitEmpty = 2, kStatusWaitQ = 4, kStatusWaitTask = 8,
-             kStatusStaticCycle = 16 };
+             kStatusStaticCycle = 16, kStatusWaitDesc = 32 };
 
 struct StageHdr {
-  int request, split, group, ntok, flags, count_r, qslot, pad;
+  int request, split, group, ntok, flags, count_r, t0, pad;
 };
 
 struct TaskDesc {
@@ -62,59 +64,92 @@ struct TaskDesc {
 
 template <int D, int NT>
 struct Cfg {
+  static constexpr bool kBig = D * NT >= 512;            // D=256 with a 16-row group
   static constexpr int kConsumerWarps = 4;
-  static constexpr int kProducerWarp = 4;   // warp 5 is the scheduler
-  static constexpr int kThreads = 6 * 32;
+  // One warp's cp.async issue rate caps its bandwidth, so the copies are spread over
+  // as many producer warps as the register file allows next to the consumers.
+  static constexpr int kProducerWarps = kBig ? 2 : (NT == 2 ? 5 : 6);
+  static constexpr int kProducerWarp0 = kConsumerWarps;
+  static constexpr int kIndexerWarp = kProducerWarp0 + kProducerWarps;
+  static constexpr int kSchedulerWarp = kIndexerWarp + 1;
+  static constexpr int kWarps = kSchedulerWarp + 1;
+  static constexpr int kThreads = kWarps * 32;
   static constexpr int kConsumerThreads = kConsumerWarps * 32;
   static constexpr int kTS = 64;                         // tokens per stage
   static constexpr int kRowBytes = D * 2;
-  static constexpr int kChunks = kRowBytes / 16;         // 16-byte chunks per row
+  static constexpr int kChunks = D / 8;                  // 16-byte chunks per row
   static constexpr int kTPI = (32 / kChunks) > 0 ? 32 / kChunks : 1;  // tokens per warp copy
   static constexpr int kTileBytes = kTS * kRowBytes;
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kQRows = NT * 8;
   static constexpr int kQBytes = kQRows * kRowBytes;
   static constexpr int kRedStride = D + 4;               // floats; padding avoids bank conflicts
-  static constexpr int kRedBytes = kConsumerWarps * kQRows * kRedStride * 4;
+  static constexpr int kRedOne = kConsumerWarps * kQRows * kRedStride * 4;
   static constexpr int kTaskQ = 4;
+  static constexpr int kSD = kBig ? 6 : 12;              // stage-descriptor ring depth
+  static constexpr int kNB = 4;                          // stages indexed per round trip
+  static constexpr int kSDEntry = kTS * 24;              // koff, voff (int64), page, row (int32)
+  static constexpr int kSDBytes = kSD * kSDEntry;
   static constexpr int kMiscBytes = 4096;
-  static constexpr int kFixed = 2 * kQBytes + kRedBytes + kMiscBytes;
+  static constexpr int kFixed1 = 2 * kQBytes + kSDBytes + kMiscBytes;
+  static constexpr int kRedBufs = (kFixed1 + 2 * kRedOne + 3 * kStageBytes <= kSmemBudget) ? 2 : 1;
+  static constexpr int kFixed = kFixed1 + kRedBufs * kRedOne;
   static constexpr int kStagesRaw = (kSmemBudget - kFixed) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static_assert(kStages >= 2, "shared memory budget too small");
-  // Offsets.
+  // Offsets from the 1024-byte aligned base (tiles first: they need the alignment).
   static constexpr int kOffQ = kStages * kStageBytes;
   static constexpr int kOffRed = kOffQ + 2 * kQBytes;
-  static constexpr int kOffMisc = kOffRed + kRedBytes;
-  static constexpr int kSmemBytes = kOffMisc + kMiscBytes;
+  static constexpr int kOffSD = kOffRed + kRedBufs * kRedOne;
+  static constexpr int kOffMisc = kOffSD + kSDBytes;
+  static constexpr int kSmemUsed = kOffMisc + kMiscBytes;
+  static constexpr int kSmemBytes = kSmemUsed + 1024;    // launch size including alignment slack
+  static_assert(kSmemUsed <= kSmemBudget, "shared memory budget exceeded");
+  static_assert(kTileBytes % 1024 == 0 && kQBytes % 1024 == 0, "tiles must keep 1024-byte alignment");
 };
 
-// Small shared-memory area: barriers, stage headers, task queue, reduction scalars.
-template <int D, int NT>
+// Barriers, ring headers and the per-warp softmax statistics of the epilogue.
 struct Misc {
-  uint64_t full[8], empty[8], qfull[2], qempty[2], tfull[4], tempty[4];
+  uint64_t full[8], empty[8], qfull[2], qempty[2], tfull[4], tempty[4], sfull[12], sempty[12], join[2],
+      drain;
   StageHdr hdr[8];
+  StageHdr shdr[12];
   TaskDesc tq[4];
-  float m[4][16], l[4][16], gm[16], gl[16];
-  int flag;
+  float m[2][4][16], l[2][4][16];
 };
 
-// Byte offset of 16-byte chunk `chunk` inside row `row` of a tile: the low three chunk
-// bits are XORed with the row so eight consecutive rows at one logical chunk hit eight
-// distinct bank groups (conflict-free ldmatrix).
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {
-  return static_cast<uint32_t>((chunk ^ (row & 7)) << 4);
+// Byte offset of 16-byte chunk `chunk` of row `row` in a tile of ROWS rows laid out
+// [D/64][ROWS][128 B] with the 128-byte swizzle (chunk bits 0-2 XOR row bits 0-2).
+template <int ROWS>
+__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
+  return static_cast<uint32_t>(((chunk >> 3) * ROWS + row) * 128 + (((chunk & 7) ^ (row & 7)) << 4));
 }
 
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// Bounded wait that also reconverges the warp (the callers run warp-collective code next).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+  const bool ok = mbar_wait(bar, parity, global_timer_ns() + kWaitLimitNs);
+  __syncwarp();
+  if (!ok && (threadIdx.x & 31) == 0) atomicOr(status, code);
+  return ok;
+}
+
+// Bounded join of the four consumer warps on an mbarrier (count 4, one arrival per
+// warp); unlike a named barrier it cannot hang if a warp has unwound after a timeout.
+__device__ __forceinline__ bool consumer_join(uint64_t* bar, uint32_t parity, int* status) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+  return warp_wait(bar, parity, status, kStatusWaitFull);
+}
 
 template <typename T, int D, int NT>
 struct Kernel {
   using C = Cfg<D, NT>;
-  using M = Misc<D, NT>;
+  static_assert(sizeof(Misc) <= C::kMiscBytes, "misc area too small");
 
-  // ------------------------------------------------------------------ scheduler
-  __device__ static bool push_task(M& ms, int& ti, uint32_t& tph, const TaskDesc& t, int* status) {
+  // ------------------------------------------------------------------ scheduler (lane 0)
+  __device__ static bool push_task(Misc& ms, int& ti, uint32_t& tph, const TaskDesc& t, int* status) {
     if (!mbar_wait(&ms.tempty[ti], tph ^ 1u, global_timer_ns() + kWaitLimitNs)) {
       atomicOr(status, kStatusWaitTask);
       return false;
@@ -128,7 +163,7 @@ struct Kernel {
     return true;
   }
 
-  __device__ static void scheduler(const DecodeLaunch& a, M& ms) {
+  __device__ static void scheduler(const DecodeLaunch& a, Misc& ms) {
     const sgld_plan_buffers& p = a.p;
     const int G = a.d.kv_heads;
     const int W = gridDim.x, worker = blockIdx.x;
@@ -205,269 +240,287 @@ struct Kernel {
     push_task(ms, ti, tph, end_marker, a.d.status);
   }
 
-  // ------------------------------------------------------------------ producer
-  struct Job {
+  // ------------------------------------------------------------------ indexer (warp)
+  // Ring entry layout: koff[kTS], voff[kTS] (int64 element offsets of the rows, without
+  // the dim term), then page[kTS], row[kTS] (int32, paged TMA coordinates).
+  struct Batch {
     TaskDesc t;
-    int t0;
-    int first;
+    int tb;       // first token of the batch
+    int phys[C::kNB][2], inner[C::kNB][2];
   };
 
-  __device__ static bool pop_task(M& ms, int& ti, uint32_t& tph, TaskDesc& t, int* status) {
+  // Issue the index loads of up to kNB stages starting at token tb (tokens past the
+  // task's end are clamped to its last token so every index read stays in bounds).
+  __device__ static void gather(const DecodeLaunch& a, Batch& b) {
     const int lane = threadIdx.x & 31;
-    const bool ok = mbar_wait(&ms.tfull[ti], tph, global_timer_ns() + kWaitLimitNs);
-    __syncwarp();
-    if (!ok) {
-      if (lane == 0) atomicOr(status, kStatusWaitTask);
-      return false;
+    const int ps = a.d.page_size;
+#pragma unroll
+    for (int i = 0; i < C::kNB; ++i) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int tok = min(b.tb + i * C::kTS + h * 32 + lane, b.t.end - 1);
+        if (a.csr) {
+          b.phys[i][h] = __ldg(a.d.pages + b.t.base + tok);
+          b.inner[i][h] = 0;
+        } else {
+          const int page = tok / ps;
+          b.phys[i][h] = __ldg(a.d.pages + static_cast<int64_t>(b.t.base) * a.d.pt_stride[0] +
+                               static_cast<int64_t>(page) * a.d.pt_stride[1]);
+          b.inner[i][h] = tok - page * ps;
+        }
+      }
     }
-    t = ms.tq[ti];
+  }
+
+  // Next batch after `cur`: the rest of the same task, or the first batch of the next
+  // task from the task ring.  Returns false at the end of the work (or on a timeout).
+  __device__ static bool next_batch(Misc& ms, const Batch& cur, bool have_cur, Batch& nxt, int& ti,
+                                    uint32_t& tph, int* status) {
+    const int lane = threadIdx.x & 31;
+    if (have_cur && cur.tb + C::kNB * C::kTS < cur.t.end) {
+      nxt.t = cur.t;
+      nxt.tb = cur.tb + C::kNB * C::kTS;
+      return true;
+    }
+    if (!warp_wait(&ms.tfull[ti], tph, status, kStatusWaitTask)) return false;
+    nxt.t = ms.tq[ti];
     __syncwarp();
     if (lane == 0) mbar_arrive(&ms.tempty[ti]);
     if (++ti == C::kTaskQ) {
       ti = 0;
       tph ^= 1u;
     }
-    return true;
+    nxt.tb = nxt.t.begin;
+    return nxt.t.valid != 0;
   }
 
-  // Row index of token `tok` of the job's request: CSR -> kv_indices row,
-  // paged -> physical page.  Issued one stage ahead of its use.
-  __device__ static void prefetch(const DecodeLaunch& a, const Job& j, int (&phys)[2]) {
+  __device__ static void indexer(const DecodeLaunch& a, unsigned char* smem, Misc& ms) {
     const int lane = threadIdx.x & 31;
+    int* status = a.d.status;
+    const int64_t* ks = a.d.k_stride;
+    const int64_t* vs = a.d.v_stride;
+    int ti = 0, sd = 0;
+    uint32_t tph = 0, sph = 0;
+    Batch b, n;
+    bool have = next_batch(ms, b, false, b, ti, tph, status);
+    if (have) gather(a, b);
+    bool ok = true;
+    while (have && ok) {
+      // Put the next batch's loads in flight before writing this one (they land while
+      // this batch waits for free descriptor slots).
+      const bool have_next = next_batch(ms, b, true, n, ti, tph, status);
+      if (have_next) gather(a, n);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int tok = min(j.t0 + h * 32 + lane, j.t.end - 1);
-      if (a.csr) {
-        phys[h] = __ldg(a.d.pages + j.t.base + tok);
-      } else {
-        const int ps = a.d.page_size;
-        phys[h] = __ldg(a.d.pages + static_cast<int64_t>(j.t.base) * a.d.pt_stride[0] +
-                        static_cast<int64_t>(tok / ps) * a.d.pt_stride[1]);
+      for (int i = 0; i < C::kNB; ++i) {
+        const int t0 = b.tb + i * C::kTS;
+        if (t0 >= b.t.end) break;
+        ok = warp_wait(&ms.sempty[sd], sph ^ 1u, status, kStatusWaitDesc);
+        if (!ok) break;
+        unsigned char* entry = smem + C::kOffSD + sd * C::kSDEntry;
+        int64_t* koff = reinterpret_cast<int64_t*>(entry);
+        int64_t* voff = koff + C::kTS;
+        int* page = reinterpret_cast<int*>(voff + C::kTS);
+        int* row = page + C::kTS;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int64_t pr = b.phys[i][h], in = b.inner[i][h];
+          const int j = h * 32 + lane;
+          koff[j] = pr * ks[0] + in * ks[1] + static_cast<int64_t>(b.t.group) * ks[2];
+          voff[j] = pr * vs[0] + in * vs[1] + static_cast<int64_t>(b.t.group) * vs[2];
+          page[j] = b.phys[i][h];
+          row[j] = b.inner[i][h];
+        }
+        if (lane == 0) {
+          StageHdr h;
+          h.request = b.t.request;
+          h.split = b.t.split;
+          h.group = b.t.group;
+          h.ntok = min(C::kTS, b.t.end - t0);
+          h.flags = (t0 == b.t.begin ? kFlagFirst : 0) | (t0 + C::kTS >= b.t.end ? kFlagLast : 0);
+          h.count_r = b.t.count_r;
+          h.t0 = t0;
+          h.pad = 0;
+          ms.shdr[sd] = h;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ms.sfull[sd]);
+        if (++sd == C::kSD) {
+          sd = 0;
+          sph ^= 1u;
+        }
       }
+      have = have_next;
+      b = n;
     }
+    if (!ok) return;
+    if (!warp_wait(&ms.sempty[sd], sph ^ 1u, status, kStatusWaitDesc)) return;
+    if (lane == 0) {
+      StageHdr h{};
+      h.flags = kFlagExit;
+      ms.shdr[sd] = h;
+      mbar_arrive(&ms.sfull[sd]);
+    }
+    __syncwarp();
   }
 
-  __device__ static void load_q(const DecodeLaunch& a, const TaskDesc& t, unsigned char* qdst,
-                                uint64_t* bar) {
+  // ------------------------------------------------------------------ producers (P warps)
+  __device__ static void load_q(const DecodeLaunch& a, const StageHdr& h, unsigned char* qdst, uint64_t* bar) {
     const int lane = threadIdx.x & 31;
     const T* q = static_cast<const T*>(a.d.q);
-    const int group_size = a.group_size;
-    const uint32_t dst0 = smem_addr(qdst);
+    const int gs = a.group_size;
+    const T* qrow0 = q + static_cast<int64_t>(h.request) * a.d.q_stride[0] +
+                     static_cast<int64_t>(h.group * gs) * a.d.q_stride[1];
     if (a.fast_q) {
+      const uint32_t dst0 = smem_addr(qdst);
       for (int idx = lane; idx < C::kQRows * C::kChunks; idx += 32) {
-        const int h = idx / C::kChunks, c = idx % C::kChunks;
-        const bool live = h < group_size;
-        const T* src = q + static_cast<int64_t>(t.request) * a.d.q_stride[0] +
-                       static_cast<int64_t>(t.group * group_size + (live ? h : 0)) * a.d.q_stride[1] + c * 8;
-        cp_async_16_fill(dst0 + h * C::kRowBytes + swz(h, c), src, live ? 16u : 0u);
+        const int r = idx / C::kChunks, c = idx % C::kChunks;
+        const bool live = r < gs;   // rows past the group read as zeros
+        const T* src = qrow0 + static_cast<int64_t>(live ? r : 0) * a.d.q_stride[1] + c * 8;
+        cp_async_16_fill(dst0 + tile_off<C::kQRows>(r, c), src, live ? 16u : 0u);
       }
       cp_async_arrive_noinc(bar);
     } else {
       for (int idx = lane; idx < C::kQRows * D; idx += 32) {
-        const int h = idx / D, d = idx % D;
+        const int r = idx / D, d = idx % D;
         T v = from_float<T>(0.f);
-        if (h < group_size) {
-          v = q[static_cast<int64_t>(t.request) * a.d.q_stride[0] +
-                static_cast<int64_t>(t.group * group_size + h) * a.d.q_stride[1] +
-                static_cast<int64_t>(d) * a.d.q_stride[2]];
-        }
-        *reinterpret_cast<T*>(qdst + h * C::kRowBytes + swz(h, d >> 3) + (d & 7) * 2) = v;
+        if (r < gs) v = qrow0[static_cast<int64_t>(r) * a.d.q_stride[1] + static_cast<int64_t>(d) * a.d.q_stride[2]];
+        *reinterpret_cast<T*>(qdst + tile_off<C::kQRows>(r, d >> 3) + (d & 7) * 2) = v;
       }
       mbar_arrive(bar);
     }
   }
 
-  __device__ static void issue_stage(const DecodeLaunch& a, const Job& j, const int (&phys)[2],
-                                     unsigned char* stage, uint64_t* bar) {
+  __device__ static void producer(const DecodeLaunch& a, unsigned char* smem, Misc& ms) {
     const int lane = threadIdx.x & 31;
+    const int pw = (threadIdx.x >> 5) - C::kProducerWarp0;   // 0 .. P-1
+    int* status = a.d.status;
     const T* kbase = static_cast<const T*>(a.d.k);
     const T* vbase = static_cast<const T*>(a.d.v);
-    const int64_t* ks = a.d.k_stride;
-    const int64_t* vs = a.d.v_stride;
-    const int ps = a.d.page_size;
-    const int group = j.t.group;
-    const uint32_t kdst = smem_addr(stage);
-    const uint32_t vdst = kdst + C::kTileBytes;
-    if (a.fast_kv) {
-#pragma unroll
-      for (int i = 0; i < C::kTS / C::kTPI; ++i) {
-        const int jt = i * C::kTPI + lane / C::kChunks;   // token within the stage
-        const int c = lane % C::kChunks;
-        const int ph = __shfl_sync(0xffffffffu, phys[(i * C::kTPI) >> 5], jt & 31);
-        const int tok = min(j.t0 + jt, j.t.end - 1);
-        const int inner = a.csr ? 0 : tok % ps;
-        const int64_t koff = static_cast<int64_t>(ph) * ks[0] + static_cast<int64_t>(inner) * ks[1] +
-                             static_cast<int64_t>(group) * ks[2] + c * 8;
-        const int64_t voff = static_cast<int64_t>(ph) * vs[0] + static_cast<int64_t>(inner) * vs[1] +
-                             static_cast<int64_t>(group) * vs[2] + c * 8;
-        const uint32_t off = jt * C::kRowBytes + swz(jt, c);
-        cp_async_16(kdst + off, kbase + koff);
-        cp_async_16(vdst + off, vbase + voff);
-      }
-      cp_async_arrive_noinc(bar);
-    } else {
-      // Generic strides: element loads into the same swizzled layout.
-      for (int jt = 0; jt < C::kTS; ++jt) {
-        const int ph = __shfl_sync(0xffffffffu, phys[jt >> 5], jt & 31);
-        const int tok = min(j.t0 + jt, j.t.end - 1);
-        const int inner = a.csr ? 0 : tok % ps;
-        const int64_t krow = static_cast<int64_t>(ph) * ks[0] + static_cast<int64_t>(inner) * ks[1] +
-                             static_cast<int64_t>(group) * ks[2];
-        const int64_t vrow = static_cast<int64_t>(ph) * vs[0] + static_cast<int64_t>(inner) * vs[1] +
-                             static_cast<int64_t>(group) * vs[2];
-        unsigned char* krow_s = stage + jt * C::kRowBytes;
-        unsigned char* vrow_s = krow_s + C::kTileBytes;
-        for (int d = lane; d < D; d += 32) {
-          const uint32_t o = swz(jt, d >> 3) + (d & 7) * 2;
-          *reinterpret_cast<T*>(krow_s + o) = kbase[krow + static_cast<int64_t>(d) * ks[3]];
-          *reinterpret_cast<T*>(vrow_s + o) = vbase[vrow + static_cast<int64_t>(d) * vs[3]];
-        }
-      }
-      mbar_arrive(bar);
-    }
-  }
-
-  __device__ static void producer(const DecodeLaunch& a, unsigned char* smem, M& ms) {
-    const int lane = threadIdx.x & 31;
-    int ti = 0;
-    uint32_t tph = 0;
-    int s = 0;
-    uint32_t ph = 0;
-    int qcount = 0;
-    int* status = a.d.status;
-    Job cur{}, nxt{};
-    int cidx[2] = {0, 0}, nidx[2] = {0, 0};
-    bool have = pop_task(ms, ti, tph, cur.t, status) && cur.t.valid;
-    cur.t0 = have ? cur.t.begin : 0;
-    cur.first = 1;
-    if (have) prefetch(a, cur, cidx);
-    bool aborted = false;
-    while (have) {
-      // Advance: next stage of this task, or the first stage of the next task.
-      bool nhave;
-      if (cur.t0 + C::kTS < cur.t.end) {
-        nxt = cur;
-        nxt.t0 = cur.t0 + C::kTS;
-        nxt.first = 0;
-        nhave = true;
-      } else {
-        // A failed pop (bounded wait expired, status already set) ends the stream.
-        nhave = pop_task(ms, ti, tph, nxt.t, status) && nxt.t.valid;
-        nxt.t0 = nhave ? nxt.t.begin : 0;
-        nxt.first = 1;
-      }
-      if (nhave) prefetch(a, nxt, nidx);
-      if (cur.first) {
+    int sd = 0, s = 0, qcount = 0;
+    uint32_t sph = 0, ph = 0;
+    bool ok = true;
+    while (true) {
+      ok = warp_wait(&ms.sfull[sd], sph, status, kStatusWaitDesc);
+      if (!ok) break;
+      const StageHdr h = ms.shdr[sd];
+      if (h.flags & kFlagExit) break;
+      if ((h.flags & kFlagFirst) && pw == 0) {
         const int qs = qcount & 1;
-        const bool qok = mbar_wait(&ms.qempty[qs], ((qcount >> 1) & 1) ^ 1u, global_timer_ns() + kWaitLimitNs);
-        __syncwarp();
-        if (!qok) {
-          if (lane == 0) atomicOr(status, kStatusWaitQ);
-          aborted = true;
-          break;
+        ok = warp_wait(&ms.qempty[qs], ((qcount >> 1) & 1) ^ 1u, status, kStatusWaitQ);
+        if (!ok) break;
+        load_q(a, h, smem + C::kOffQ + qs * C::kQBytes, &ms.qfull[qs]);
+      }
+      if (h.flags & kFlagFirst) ++qcount;
+      ok = warp_wait(&ms.empty[s], ph ^ 1u, status, kStatusWaitEmpty);
+      if (!ok) break;
+      const unsigned char* entry = smem + C::kOffSD + sd * C::kSDEntry;
+      const int64_t* koff = reinterpret_cast<const int64_t*>(entry);
+      const int64_t* voff = koff + C::kTS;
+      const int* page = reinterpret_cast<const int*>(voff + C::kTS);
+      const int* prow = page + C::kTS;
+      unsigned char* stage = smem + s * C::kStageBytes;
+      const uint32_t kdst = smem_addr(stage);
+      const uint32_t vdst = kdst + C::kTileBytes;
+      if (a.tma_kv) {
+        // Tensor-map boxes: {64 dims, 1 head, R rows of one page}; only producer 0 issues.
+        if (pw == 0 && lane == 0) {
+          const int R = a.box_rows;
+          const int nchunks = (h.ntok + R - 1) / R;
+          ms.hdr[s] = h;
+          mbar_arrive_expect_tx(&ms.full[s], static_cast<uint32_t>(nchunks * R * C::kRowBytes * 2));
+          for (int c = 0; c < nchunks; ++c) {
+            const int j = c * R;   // the box never crosses a page (R divides the page size)
+#pragma unroll
+            for (int part = 0; part < D / 64; ++part) {
+              const uint32_t off = static_cast<uint32_t>((part * C::kTS + j) * 128);
+              tma_load_4d(kdst + off, &a.kmap, part * 64, h.group, prow[j], page[j], &ms.full[s]);
+              tma_load_4d(vdst + off, &a.vmap, part * 64, h.group, prow[j], page[j], &ms.full[s]);
+            }
+          }
         }
-        load_q(a, cur.t, smem + C::kOffQ + qs * C::kQBytes, &ms.qfull[qs]);
-        ++qcount;
-      }
-      const bool eok = mbar_wait(&ms.empty[s], ph ^ 1u, global_timer_ns() + kWaitLimitNs);
-      __syncwarp();
-      if (!eok) {
-        if (lane == 0) atomicOr(status, kStatusWaitEmpty);
-        aborted = true;
-        break;
-      }
-      issue_stage(a, cur, cidx, smem + s * C::kStageBytes, &ms.full[s]);
-      if (lane == 0) {
-        StageHdr h;
-        h.request = cur.t.request;
-        h.split = cur.t.split;
-        h.group = cur.t.group;
-        h.ntok = min(C::kTS, cur.t.end - cur.t0);
-        h.flags = (cur.first ? kFlagFirst : 0) | (cur.t0 + C::kTS >= cur.t.end ? kFlagLast : 0);
-        h.count_r = cur.t.count_r;
-        h.qslot = (qcount - 1) & 1;
-        h.pad = 0;
-        ms.hdr[s] = h;
+        __syncwarp();
+        mbar_arrive(&ms.full[s]);   // 32P plain arrivals + the expect_tx arrival above
+      } else if (a.fast_kv) {
+        // 16-byte cp.async, token pairs spread over the producer warps; tokens past the
+        // task's end are not copied (the consumers mask them).
+        const int c = lane % C::kChunks;
+#pragma unroll 4
+        for (int i = pw; i < C::kTS / C::kTPI; i += C::kProducerWarps) {
+          const int jt = i * C::kTPI + lane / C::kChunks;
+          if (jt < h.ntok) {
+            const uint32_t off = tile_off<C::kTS>(jt, c);
+            cp_async_16(kdst + off, kbase + koff[jt] + c * 8);
+            cp_async_16(vdst + off, vbase + voff[jt] + c * 8);
+          }
+        }
+        cp_async_arrive_noinc(&ms.full[s]);
+        if (pw == 0 && lane == 0) {
+          ms.hdr[s] = h;
+          mbar_arrive(&ms.full[s]);
+        }
+      } else {
+        // Generic strides: element loads into the same swizzled layout.
+        const int64_t kd = a.d.k_stride[3], vd = a.d.v_stride[3];
+        for (int jt = pw; jt < h.ntok; jt += C::kProducerWarps) {
+          const int64_t kr = koff[jt], vr = voff[jt];
+          for (int d = lane; d < D; d += 32) {
+            const uint32_t o = tile_off<C::kTS>(jt, d >> 3) + (d & 7) * 2;
+            *reinterpret_cast<T*>(stage + o) = kbase[kr + d * kd];
+            *reinterpret_cast<T*>(stage + C::kTileBytes + o) = vbase[vr + d * vd];
+          }
+        }
         mbar_arrive(&ms.full[s]);
+        if (pw == 0 && lane == 0) {
+          ms.hdr[s] = h;
+          mbar_arrive(&ms.full[s]);
+        }
       }
       __syncwarp();
+      if (lane == 0) mbar_arrive(&ms.sempty[sd]);   // this warp is done with the descriptor
+      if (++sd == C::kSD) {
+        sd = 0;
+        sph ^= 1u;
+      }
       if (++s == C::kStages) {
         s = 0;
         ph ^= 1u;
       }
-      cur = nxt;
-      cidx[0] = nidx[0];
-      cidx[1] = nidx[1];
-      have = nhave;
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    if (aborted) return;
-    // Exit marker for the consumers.
-    const bool eok = mbar_wait(&ms.empty[s], ph ^ 1u, global_timer_ns() + kWaitLimitNs);
-    __syncwarp();
-    if (!eok) {
-      if (lane == 0) atomicOr(status, kStatusWaitEmpty);
-      return;
-    }
-    if (lane == 0) {
+    if (!ok) return;
+    // Exit marker for the consumers (every producer lane arrives, producer 0 writes it).
+    if (!warp_wait(&ms.empty[s], ph ^ 1u, status, kStatusWaitEmpty)) return;
+    if (pw == 0 && lane == 0) {
       StageHdr h{};
       h.flags = kFlagExit;
       ms.hdr[s] = h;
       mbar_arrive(&ms.full[s]);
     }
-    __syncwarp();
     mbar_arrive(&ms.full[s]);
+    __syncwarp();
   }
 
-  // ------------------------------------------------------------------ consumers
-  __device__ static void write_empty_rows(const DecodeLaunch& a) {
-    const int ctid = threadIdx.x;   // 0..127
-    const int G = a.d.kv_heads, gs = a.group_size, hq = a.d.query_heads;
-    const bool err = *a.p.error != 0;
-    const T fill = from_float<T>(err ? __int_as_float(0x7fc00000) : 0.f);
-    T* out = static_cast<T*>(a.d.out);
-    for (int pair = blockIdx.x; pair < a.bcap * G; pair += gridDim.x) {
-      const int r = pair / G, g = pair % G;
-      if (__ldg(a.p.counts + r) != 0) continue;
-      T* row = out + (static_cast<int64_t>(r) * hq + g * gs) * D;
-      for (int idx = ctid; idx < gs * D; idx += C::kConsumerThreads) row[idx] = fill;
-    }
-  }
-
-  __device__ static void consumer(const DecodeLaunch& a, unsigned char* smem, M& ms) {
+  // ------------------------------------------------------------------ consumers (4 warps)
+  __device__ static void consumer(const DecodeLaunch& a, unsigned char* smem, Misc& ms) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g8 = lane >> 2;
+    const int g8 = lane >> 2, t4 = lane & 3;
     const float sc = a.d.scale * kLog2e;
     int* status = a.d.status;
-
-    write_empty_rows(a);
 
     constexpr int KS = D / 16;   // k-steps of QK == m-tiles of O^T
     uint32_t qf[NT][KS][2];
     float o[KS][NT][4];
     float m[NT][2], lsum[NT][2];
 
-    int s = 0;
+    int s = 0, task_idx = 0;
     uint32_t ph = 0;
-    int task_idx = 0;
     while (true) {
-      const bool got = mbar_wait(&ms.full[s], ph, global_timer_ns() + kWaitLimitNs);
-      __syncwarp();
-      if (!got) {
-        if (lane == 0) atomicOr(status, kStatusWaitFull);
-        return;
-      }
+      if (!warp_wait(&ms.full[s], ph, status, kStatusWaitFull)) return;
       const StageHdr h = ms.hdr[s];
-      if (h.flags & kFlagExit) return;
+      if (h.flags & kFlagExit) break;
       unsigned char* stage = smem + s * C::kStageBytes;
       if (h.flags & kFlagFirst) {
         const int qs = task_idx & 1;
-        const bool qok = mbar_wait(&ms.qfull[qs], (task_idx >> 1) & 1, global_timer_ns() + kWaitLimitNs);
-        __syncwarp();
-        if (!qok) {
-          if (lane == 0) atomicOr(status, kStatusWaitQ);
-          return;
-        }
+        if (!warp_wait(&ms.qfull[qs], (task_idx >> 1) & 1, status, kStatusWaitQ)) return;
         const uint32_t qbase = smem_addr(smem + C::kOffQ + qs * C::kQBytes);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -475,7 +528,7 @@ struct Kernel {
           for (int ks = 0; ks < KS; ks += 2) {
             const int row = nt * 8 + (lane & 7);
             const int chunk = 2 * ks + (lane >> 3);
-            ldsm_x4(qbase + row * C::kRowBytes + swz(row, chunk), qf[nt][ks][0], qf[nt][ks][1],
+            ldsm_x4(qbase + tile_off<C::kQRows>(row, chunk), qf[nt][ks][0], qf[nt][ks][1],
                     qf[nt][ks + 1][0], qf[nt][ks + 1][1]);
           }
         }
@@ -506,14 +559,14 @@ struct Kernel {
           const int row = row0 + (lane & 15);
           const int chunk = 2 * ks + (lane >> 4);
           uint32_t a0, a1, a2, a3;
-          ldsm_x4(kb + row * C::kRowBytes + swz(row, chunk), a0, a1, a2, a3);
+          ldsm_x4(kb + tile_off<C::kTS>(row, chunk), a0, a1, a2, a3);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             if (ks & 1) Mma<T>::run(sb[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
             else Mma<T>::run(sa[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
           }
         }
-        // ---- online softmax (log2 domain)
+        // ---- online softmax (log2 domain); masked tokens score -inf whatever K held
         uint32_t pb[NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -545,13 +598,23 @@ struct Kernel {
           pb[nt][0] = movmatrix_t(Mma<T>::pack(sv[0], sv[1]));
           pb[nt][1] = movmatrix_t(Mma<T>::pack(sv[2], sv[3]));
         }
-        // ---- O^T += V^T P^T
+        // ---- O^T += V^T P^T; on a partial tile the V rows past the last token are
+        //      zeroed in the fragments (their P is already zero, stale data may not be).
+        const bool partial = valid < 16;
+        const uint32_t mlo = (2 * t4 < valid ? 0x0000ffffu : 0u) | (2 * t4 + 1 < valid ? 0xffff0000u : 0u);
+        const uint32_t mhi = (2 * t4 + 8 < valid ? 0x0000ffffu : 0u) | (2 * t4 + 9 < valid ? 0xffff0000u : 0u);
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
           const int row = row0 + (lane & 7) + ((lane >> 4) << 3);
           const int chunk = 2 * mt + ((lane >> 3) & 1);
           uint32_t a0, a1, a2, a3;
-          ldsm_x4_t(vb + row * C::kRowBytes + swz(row, chunk), a0, a1, a2, a3);
+          ldsm_x4_t(vb + tile_off<C::kTS>(row, chunk), a0, a1, a2, a3);
+          if (partial) {
+            a0 &= mlo;
+            a1 &= mlo;
+            a2 &= mhi;
+            a3 &= mhi;
+          }
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) Mma<T>::run(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
         }
@@ -560,8 +623,7 @@ struct Kernel {
       if (lane == 0) mbar_arrive(&ms.empty[s]);
 
       if (h.flags & kFlagLast) {
-        __syncwarp();
-        epilogue(a, smem, ms, h, o, m, lsum);
+        if (!epilogue(a, smem, ms, h, task_idx, o, m, lsum)) return;
         ++task_idx;
       }
       if (++s == C::kStages) {
@@ -571,14 +633,18 @@ struct Kernel {
     }
   }
 
-  __device__ static void epilogue(const DecodeLaunch& a, unsigned char* smem, M& ms, const StageHdr& h,
-                                  float (&o)[D / 16][NT][4], float (&m)[NT][2], float (&lsum)[NT][2]) {
+  // Combine the four warps' (m, l, O) of one task and store the normalised partial and
+  // natural-log LSE of every query head of the group.
+  __device__ static bool epilogue(const DecodeLaunch& a, unsigned char* smem, Misc& ms, const StageHdr& h,
+                                  int task_idx, float (&o)[D / 16][NT][4], float (&m)[NT][2],
+                                  float (&lsum)[NT][2]) {
     constexpr int KS = D / 16;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, ctid = threadIdx.x;
     const int g8 = lane >> 2, t4 = lane & 3;
-    const int hq = a.d.query_heads, gs = a.group_size, smax = a.smax, G = a.d.kv_heads;
-    float* red = reinterpret_cast<float*>(smem + C::kOffRed);
-    // 1. warp-level row sums, publish per-warp (m, l)
+    const int hq = a.d.query_heads, gs = a.group_size, smax = a.smax;
+    const int buf = C::kRedBufs == 2 ? (task_idx & 1) : 0;
+    float* red = reinterpret_cast<float*>(smem + C::kOffRed + buf * C::kRedOne);
+    // 1. per-warp statistics and unscaled O^T to shared memory
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -588,31 +654,8 @@ struct Kernel {
         l += __shfl_xor_sync(0xffffffffu, l, 8);
         l += __shfl_xor_sync(0xffffffffu, l, 16);
         if (g8 == 0) {
-          ms.m[warp][nt * 8 + 2 * t4 + jj] = m[nt][jj];
-          ms.l[warp][nt * 8 + 2 * t4 + jj] = l;
-        }
-      }
-    consumer_sync();
-    // 2. combine (m, l) across warps; scale this warp's O^T into the reduction buffer
-    float scale[NT][2];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int head = nt * 8 + 2 * t4 + jj;
-        float gm = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < C::kConsumerWarps; ++w) gm = fmaxf(gm, ms.m[w][head]);
-        float gl = 0.f;
-#pragma unroll
-        for (int w = 0; w < C::kConsumerWarps; ++w) {
-          const float mw = ms.m[w][head];
-          gl += mw == -INFINITY ? 0.f : ms.l[w][head] * ex2(mw - gm);
-        }
-        scale[nt][jj] = m[nt][jj] == -INFINITY ? 0.f : ex2(m[nt][jj] - gm);
-        if (warp == 0 && g8 == 0) {
-          ms.gm[head] = gm;
-          ms.gl[head] = gl;
+          ms.m[buf][warp][nt * 8 + 2 * t4 + jj] = m[nt][jj];
+          ms.l[buf][warp][nt * 8 + 2 * t4 + jj] = l;
         }
       }
 #pragma unroll
@@ -623,72 +666,49 @@ struct Kernel {
         for (int i = 0; i < 4; ++i) {
           const int d = mt * 16 + g8 + (i >= 2 ? 8 : 0);
           const int head = nt * 8 + 2 * t4 + (i & 1);
-          red[(warp * C::kQRows + head) * C::kRedStride + d] = o[mt][nt][i] * scale[nt][i & 1];
+          red[(warp * C::kQRows + head) * C::kRedStride + d] = o[mt][nt][i];
         }
-    consumer_sync();
-    // 3. sum the four warp partials, normalise, store partial / LSE (and the output
-    //    directly when the request has a single split)
+    if (!consumer_join(&ms.join[buf], (task_idx >> (C::kRedBufs == 2 ? 1 : 0)) & 1, a.d.status)) return false;
+    // 2. one pass: rescale to the global max, sum the warps, normalise, store
     const int64_t slot0 = (static_cast<int64_t>(h.request) * hq + h.group * gs) * smax + h.split;
-    T* out = static_cast<T*>(a.d.out);
-    const int64_t orow0 = (static_cast<int64_t>(h.request) * hq + h.group * gs) * D;
     for (int idx = ctid; idx < gs * D; idx += C::kConsumerThreads) {
       const int head = idx / D, d = idx % D;
-      float v = 0.f;
+      float mw[C::kConsumerWarps];
+      float gm = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < C::kConsumerWarps; ++w) v += red[(w * C::kQRows + head) * C::kRedStride + d];
-      const float gl = ms.gl[head];
+      for (int w = 0; w < C::kConsumerWarps; ++w) {
+        mw[w] = ms.m[buf][w][head];
+        gm = fmaxf(gm, mw[w]);
+      }
+      float gl = 0.f, v = 0.f;
+#pragma unroll
+      for (int w = 0; w < C::kConsumerWarps; ++w) {
+        const float sw = mw[w] == -INFINITY ? 0.f : ex2(mw[w] - gm);
+        gl += ms.l[buf][w][head] * sw;
+        v += red[(w * C::kQRows + head) * C::kRedStride + d] * sw;
+      }
       const float res = v / gl;
       const int64_t slot = slot0 + static_cast<int64_t>(head) * smax;
       a.d.partial[slot * D + d] = res;
-      if (d == 0) a.d.lse[slot] = (ms.gm[head] + lg2(gl)) * kLn2;
-      if (h.count_r == 1) out[orow0 + idx] = from_float<T>(res);
+      if (d == 0) a.d.lse[slot] = (gm + lg2(gl)) * kLn2;
     }
-    if (h.count_r <= 1) {
-      consumer_sync();   // reduction buffers are reused by the next task
-      return;
+    if (C::kRedBufs == 1) {   // single reduction buffer: drain before the next task reuses it
+      if (!consumer_join(&ms.drain, task_idx & 1, a.d.status)) return false;
     }
-    // 4. fused merge: the CTA completing the last split of (request, kv_head) merges
-    __threadfence();
-    consumer_sync();
-    if (ctid == 0) {
-      int* counter = a.d.arrive + h.request * G + h.group;
-      const int old = atomicAdd(counter, 1);
-      const int last = old == h.count_r - 1;
-      if (last) atomicExch(counter, 0);
-      ms.flag = last;
-    }
-    consumer_sync();
-    if (ms.flag) {
-      __threadfence();
-      const int64_t base = (static_cast<int64_t>(h.request) * hq + h.group * gs) * smax;
-      for (int idx = ctid; idx < gs * D; idx += C::kConsumerThreads) {
-        const int head = idx / D, d = idx % D;
-        const int64_t hs = base + static_cast<int64_t>(head) * smax;
-        float mm = -INFINITY, den = 0.f, acc = 0.f;
-        for (int sp = 0; sp < h.count_r; ++sp) {
-          const float l = ld_cg(a.d.lse + hs + sp);
-          const float pv = ld_cg(a.d.partial + (hs + sp) * D + d);
-          const float nm = fmaxf(mm, l);
-          const float ow = ex2((mm - nm) * kLog2e);
-          const float w = ex2((l - nm) * kLog2e);
-          acc = acc * ow + pv * w;
-          den = den * ow + w;
-          mm = nm;
-        }
-        out[orow0 + idx] = from_float<T>(acc / fmaxf(den, 1.0e-30f));
-      }
-    }
-    consumer_sync();
+    return true;
   }
 
   // ------------------------------------------------------------------ entry
   __device__ static void run(const DecodeLaunch& a) {
-    extern __shared__ __align__(1024) unsigned char smem[];
-    M& ms = *reinterpret_cast<M*>(smem + C::kOffMisc);
+    extern __shared__ unsigned char smem_raw[];
+    // 1024-byte aligned base (the launch reserves 1 KB of slack): TMA's 128-byte swizzle
+    // and the tile layout assume it.
+    unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    Misc& ms = *reinterpret_cast<Misc*>(smem + C::kOffMisc);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
       for (int i = 0; i < C::kStages; ++i) {
-        mbar_init(&ms.full[i], 33);
+        mbar_init(&ms.full[i], 32 * C::kProducerWarps + 1);
         mbar_init(&ms.empty[i], C::kConsumerWarps);
       }
       for (int i = 0; i < 2; ++i) {
@@ -699,18 +719,33 @@ struct Kernel {
         mbar_init(&ms.tfull[i], 1);
         mbar_init(&ms.tempty[i], 1);
       }
+      for (int i = 0; i < C::kSD; ++i) {
+        mbar_init(&ms.sfull[i], 1);
+        mbar_init(&ms.sempty[i], C::kProducerWarps);
+      }
+      mbar_init(&ms.join[0], C::kConsumerWarps);
+      mbar_init(&ms.join[1], C::kConsumerWarps);
+      mbar_init(&ms.drain, C::kConsumerWarps);
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    // Programmatic dependent launch: everything above overlapped the previous kernel;
+    // from here on its results (the plan, the previous layer) must be visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (warp < C::kConsumerWarps) {
       consumer(a, smem, ms);
-    } else if (warp == C::kProducerWarp) {
+    } else if (warp < C::kIndexerWarp) {
       producer(a, smem, ms);
+    } else if (warp == C::kIndexerWarp) {
+      indexer(a, smem, ms);
     } else {
       if (lane == 0) scheduler(a, ms);
       __syncwarp();
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
+    // Let the dependent merge launch start filling SMs as this CTA leaves.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Exit ticket: the last CTA to finish leaves the claim counter at zero.
     if (threadIdx.x == 0) {
       __threadfence();
@@ -724,7 +759,7 @@ struct Kernel {
 };
 
 template <typename T, int D, int NT>
-__global__ void __launch_bounds__(192, 1) decode_kernel(DecodeLaunch a) {
+__global__ void __launch_bounds__(Cfg<D, NT>::kThreads, 1) decode_kernel(const __grid_constant__ DecodeLaunch a) {
   Kernel<T, D, NT>::run(a);
 }
 
@@ -738,8 +773,17 @@ cudaError_t launch_typed(const DecodeLaunch& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  decode_kernel<T, D, NT><<<a.workers, C::kThreads, C::kSmemBytes, stream>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.workers);
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NT>, a);
 }
 
 template <typename T>

@@ -1,10 +1,11 @@
 // Internal declarations shared by the kernel translation units and the C ABI.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/sgld_b200.h"
+#include "sgld_b200.h"  // include/ is on the include path (-I)
 
 namespace sgld {
 
@@ -27,19 +28,25 @@ struct PlanLaunch {
 // Host-side launchers (return a cudaError_t of the launch).
 cudaError_t launch_plan(const PlanLaunch& a, cudaStream_t stream);
 
-struct DecodeLaunch {
+// Kernel parameter block of one decode launch (passed as a __grid_constant__).
+struct alignas(64) DecodeLaunch {
+  CUtensorMap kmap;  // 4D tensor maps {D, Hkv, page_size, pages} of K and V (paged TMA path)
+  CUtensorMap vmap;
   sgld_decode_args d;
   sgld_plan_buffers p;
   int32_t bcap, smax, workers, group_size;
   int32_t csr;
   int32_t fast_kv;   // K/V rows are 16-byte aligned, unit stride along D
   int32_t fast_q;    // Q rows are 16-byte aligned, unit stride along D
+  int32_t tma_kv;    // paged KV loaded by tensor-map TMA boxes of box_rows tokens
+  int32_t box_rows;
 };
 
 cudaError_t launch_decode(const DecodeLaunch& a, cudaStream_t stream);
 
+// programmatic: launch as a programmatic dependent of the preceding kernel (PDL).
 cudaError_t launch_merge(const float* partial, const float* lse, const int32_t* counts,
                          const int32_t* error, void* out, int32_t dtype, int32_t bcap, int32_t hq,
-                         int32_t d, int32_t smax, cudaStream_t stream);
+                         int32_t d, int32_t smax, cudaStream_t stream, bool programmatic);
 
 }  // namespace sgld

@@ -1,8 +1,9 @@
 // Thin inline-PTX wrappers used by the sm_100a decode kernels.
 //
 // Everything here is a documented PTX instruction (PTX ISA 8.x): mbarrier
-// phase tracking, cp.async 16-byte copies with mbarrier completion, ldmatrix /
-// movmatrix fragment moves, mma.sync m16n8k16 and the ex2/lg2 approximations.
+// phase tracking, cp.async 16-byte copies and bulk / tensor-map (TMA) copies with
+// mbarrier completion, ldmatrix / movmatrix fragment moves, mma.sync m16n8k16 and the
+// ex2/lg2 approximations.
 // All waits are bounded by a wall-clock deadline read from %globaltimer: on
 // expiry the caller records an error status and unwinds instead of spinning.
 #pragma once
@@ -71,6 +72,32 @@ __device__ __forceinline__ void cp_async_16_fill(uint32_t dst, const void* src, 
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar))
                : "memory");
+}
+
+// ---------------------------------------------------------------- bulk copy engine (TMA)
+// Arrive on `bar` and add `bytes` to the transaction count its phase waits for.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// One-dimensional bulk copy global -> shared (16-byte aligned addresses, size a multiple
+// of 16), completing `bytes` transactions on `bar`.
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Tiled tensor-map copy of a 4D box (coordinates innermost first) into shared memory.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
+      : "memory");
 }
 
 // ---------------------------------------------------------------- fragments

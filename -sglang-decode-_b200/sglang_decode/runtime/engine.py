@@ -5,9 +5,10 @@ Same API and checks as the reference's ``runtime/engine.py:1-74``:
 ``prepare()`` (GPU plan build, once per compatible group per step) and
 ``execute(q, k, v, pages, layer=0, *, indptr=None, scale=None)`` (paged
 ``[page, token, head, dim]`` or CSR ``[token, head, dim]`` KV, arbitrary strides).
-``execute`` is ONE launch of the sm_100a persistent decode kernel with the split
-merge fused in; the claim counter is reset by the plan build and left at zero by
-the decode launch itself (the reference's per-layer memset is not needed).
+``execute`` enqueues the sm_100a persistent decode kernel and the split merge (a
+programmatic dependent launch that overlaps the decode's tail); the claim counter is
+reset by the plan build and left at zero by the decode launch itself (the
+reference's per-layer memset is not needed).
 """
 from dataclasses import dataclass
 
@@ -93,12 +94,13 @@ class DecodeEngine:
             a.page_size = 1
         a.q, a.k, a.v, a.out, a.pages = (q.data_ptr(), k.data_ptr(), v.data_ptr(),
                                          out.output.data_ptr(), pages.data_ptr())
+        a.kv_extent = k.shape[0] if k.shape[0] == v.shape[0] else 0
         a.q_stride[:] = q.stride()
         a.dtype = _DTYPES[q.dtype]
         a.query_heads, a.kv_heads, a.head_dim = c.query_heads, c.kv_heads, c.head_dim
         a.scale = c.head_dim ** -0.5 if scale is None else float(scale)
         a.counter, a.partial, a.lse = out.counter.data_ptr(), out.partial.data_ptr(), out.lse.data_ptr()
-        a.arrive, a.status = out.arrive.data_ptr(), out.status.data_ptr()
+        a.status = out.status.data_ptr()
         stream = torch.cuda.current_stream(p.device).cuda_stream
         _native.decode_persistent(a, p.c_buffers, p.c_geometry, stream)
         return out.output

@@ -2,10 +2,9 @@
 
 Same buffers and attribute names as the reference's ``runtime/workspace.py:1-40``:
 ``PlanBuffers`` holds the int32 SoA plan arrays and ``LayerBuffers`` the per-layer
-claim counter, fp32 partial/LSE split slots and the output.  Additions needed by the
-fused decode kernel: ``LayerBuffers.arrive`` (per (request, kv_head) split-arrival
-counters, self-resetting) and ``LayerBuffers.status`` (bounded-wait error word);
-``counter`` has two words (claim counter + exit ticket).
+claim counter, fp32 partial/LSE split slots and the output.  Additions of the B200
+kernel: ``LayerBuffers.status`` (bounded-wait error word); ``counter`` has two words
+(claim counter + exit ticket).
 """
 from dataclasses import dataclass, field
 
@@ -71,7 +70,6 @@ class LayerBuffers:
     partial: torch.Tensor
     lse: torch.Tensor
     output: torch.Tensor
-    arrive: torch.Tensor = None
     status: torch.Tensor = None
     c_args: object = field(default=None, repr=False)
 
@@ -85,6 +83,5 @@ class LayerBuffers:
                    torch.empty(shape, dtype=torch.float32, device=device),
                    torch.empty((config.batch_capacity, config.query_heads, config.head_dim),
                                dtype=dtype, device=device),
-                   torch.zeros(config.batch_capacity * config.kv_heads, dtype=torch.int32, device=device),
                    torch.zeros(1, dtype=torch.int32, device=device),
                    _native.DecodeArgs())

@@ -156,6 +156,20 @@ def baseline(name, seed=17, workers=148):
     raise KeyError(name)
 
 
+def subset(b: Baseline, requests: int) -> Baseline:
+    """The first ``requests`` requests of a Baseline (pool sized for them), same config."""
+    import dataclasses
+    lengths = b.lengths[:requests]
+    c = b.config
+    if b.csr:
+        pool_tokens = b.pool_tokens if b.name == "C1" else sum(lengths) + (b.pool_tokens - sum(b.lengths))
+        return dataclasses.replace(b, lengths=lengths, pool_tokens=max(pool_tokens, sum(lengths), 1))
+    pages = sum(math.ceil(n / c.page_size) for n in lengths)
+    if b.name == "C4":
+        pages = math.ceil(1.1 * pages)
+    return dataclasses.replace(b, lengths=lengths, pool_pages=max(pages, 1))
+
+
 def paged_tables(config, lengths, pool_pages, generator, device):
     """Page table [Bcap, max_pages] from consecutive slices of a page permutation."""
     perm = torch.randperm(pool_pages, generator=generator, device=device)

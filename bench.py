@@ -50,6 +50,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="C3", choices=["C1", "C2", "C3", "C4"])
     ap.add_argument("--mode", type=int, default=-1, help="-1 AUTO, 0..4 force a mode")
+    ap.add_argument("--requests", type=int, default=None,
+                    help="profile a prefix sub-workload (first N requests); not a bench line")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
@@ -229,7 +231,7 @@ def run_ours(args):
 
     from sglang_decode.config import DecodeConfig
     from sglang_decode.runtime.engine import DecodeEngine
-    from sglang_decode.workloads import baseline, generate, update_plan
+    from sglang_decode.workloads import baseline, generate, subset, update_plan
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -243,6 +245,8 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     b = baseline(args.workload, workers=sms)
+    if args.requests is not None:
+        b = subset(b, args.requests)
     c = b.config
     if c.kv_heads % world:
         raise SystemExit(f"{c.kv_heads} KV heads do not shard over {world} GPUs")

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define SGLD_ABI_VERSION 1
+#define SGLD_ABI_VERSION 3
 
 typedef enum sgld_status {
   SGLD_OK = 0,
@@ -104,6 +104,8 @@ typedef struct sgld_decode_args {
   int64_t k_stride[4];  /* (page, token-in-page, head, dim); CSR: (token, 0, head, dim)      */
   int64_t v_stride[4];
   int64_t pt_stride[2]; /* page table strides (paged only)                                   */
+  int64_t kv_extent;    /* paged: pages in k/v; CSR: token slots in k/v; 0 if unknown. Bounds
+                           the tensor-map (TMA) copies of the paged path                      */
   int32_t dtype;        /* SGLD_DTYPE_*                                                      */
   int32_t query_heads;  /* Hq on this GPU                                                    */
   int32_t kv_heads;     /* Hkv on this GPU (== plan groups)                                  */
@@ -114,20 +116,20 @@ typedef struct sgld_decode_args {
   int32_t* counter;     /* [2]  claim counter + exit ticket; zero before, left zero after    */
   float* partial;       /* [B, Hq, Smax, D] fp32 normalised split outputs                    */
   float* lse;           /* [B, Hq, Smax]    fp32 natural-log LSE per split                   */
-  int32_t* arrive;      /* [B * Hkv] split-arrival counters; zero before, left zero after    */
   int32_t* status;      /* [1]  0 = ok; bounded in-kernel wait expired otherwise (sticky)    */
 } sgld_decode_args;
 
 /*
- * Persistent paged GQA decode with the split merge fused in (one launch, W CTAs).
+ * Persistent paged GQA decode followed by the split merge (two launches: W decode
+ * CTAs, then the merge grid as a programmatic dependent launch).
  * Replaces reference runtime/engine.py:62-73: the counter reset, the
  * persistent_decode launch (kernels/attention.py:87-130, task body :12-84) and
  * the merge_splits launch (kernels/merge.py:7-30).  Task dispatch follows
  * plan->mode exactly (R0 prefix search, R1 stride, STATIC lists, D1/D4 atomic
  * pack claims); each task writes its normalised partial and LSE to slot
- * (request*Hq + head)*Smax + split; the CTA finishing a request's last split
- * merges that request's splits in split order into `out`.  Rows with no record
- * are written as zeros, or NaN when plan->error is set.
+ * (request*Hq + head)*Smax + split; the merge combines each row's splits in split
+ * order into `out`.  Rows with no record are written as zeros, or NaN when
+ * plan->error is set.
  */
 int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers* plan,
                            const sgld_plan_geometry* geometry, void* stream);
@@ -140,7 +142,7 @@ int sgld_merge_splits(const float* partial, const float* lse, const int32_t* cou
                       const int32_t* error, void* out, int32_t dtype, int32_t batch_capacity,
                       int32_t query_heads, int32_t head_dim, int32_t max_splits, void* stream);
 
-/* Bytes of per-layer scratch (counter, partial, lse, arrive, status) for one decode
+/* Bytes of per-layer scratch (counter, partial, lse, status) for one decode
  * layer -- reference runtime/workspace.py:33-40 (LayerBuffers.allocate). */
 size_t sgld_layer_workspace_bytes(int32_t batch_capacity, int32_t query_heads, int32_t kv_heads,
                                   int32_t head_dim, int32_t max_splits);

@@ -36,7 +36,6 @@ def run(engine, inputs, lengths, splits=None, indptr=None, layer=0, scale=None):
     torch.cuda.synchronize()
     assert lb.status.item() == 0, "bounded in-kernel wait expired"
     assert engine.counters.eq(0).all(), "claim counter / exit ticket not left at zero"
-    assert lb.arrive.eq(0).all(), "split arrival counters not left at zero"
     return out
 
 
