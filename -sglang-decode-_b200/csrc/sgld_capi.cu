@@ -115,6 +115,11 @@ int check_plan_pointers(const sgld_plan_buffers* p) {
 
 }  // namespace
 
+namespace sgld {
+// Record `msg` as this host thread's sgld_last_error() message and return `code`.
+int set_last_error(int code, const char* msg) { return fail(code, msg); }
+}  // namespace sgld
+
 extern "C" {
 
 int32_t sgld_abi_version(void) { return SGLD_ABI_VERSION; }

@@ -44,6 +44,9 @@ struct alignas(64) DecodeLaunch {
 
 cudaError_t launch_decode(const DecodeLaunch& a, cudaStream_t stream);
 
+// Record `msg` as the calling host thread's sgld_last_error() message; returns `code`.
+int set_last_error(int code, const char* msg);
+
 // programmatic: launch as a programmatic dependent of the preceding kernel (PDL).
 cudaError_t launch_merge(const float* partial, const float* lse, const int32_t* counts,
                          const int32_t* error, void* out, int32_t dtype, int32_t bcap, int32_t hq,

@@ -1,0 +1,89 @@
+// sgld_decode_persistent_noalloc: the decode + merge of sgld_decode_persistent for
+// callers that cannot allocate device memory.
+//
+// Some hosts hand the library only the input and output buffers of a call and cannot
+// provide per-layer scratch: plugin interfaces whose signature carries no workspace, or
+// servers that give all free device memory to their KV-cache pool at start-up and allow
+// no allocation afterwards (cudaMalloc also synchronises the device, which a serving
+// loop cannot afford).  For them the scratch of the decode -- the claim counter and exit
+// ticket, the status word, and the fp32 partial outputs and LSEs of every split slot --
+// lives in one file-scope device array of kScratchBytes bytes, reserved on every GPU
+// that loads the library until the process exits.
+//
+// Host code only sees a stand-in for the array's name, never its device address: the
+// address is obtained once per device with cudaGetSymbolAddress (with that device
+// current) on the first call made on that device, and passed to the kernels.  Make that
+// first call before any stream capture.  The entry point allocates and frees nothing.
+//
+// Every call shares the one array and leaves its last contents there.  Each call clears
+// the words that must start at zero (counter, exit ticket, status) on its stream before
+// the decode; calls whose GPU work overlaps (different streams, or several threads)
+// race on the array and must be serialised by the caller.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "sgld_internal.cuh"
+
+namespace {
+
+constexpr size_t kScratchBytes = size_t{16} << 20;   // 16 MiB per GPU
+constexpr size_t kHeaderBytes = 256;                  // counter[2], status, padding
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
+
+std::mutex g_setup_mutex;
+void* g_scratch_addr[kMaxDevices] = {};
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace
+
+extern "C" int sgld_decode_persistent_noalloc(const sgld_decode_args* args, const sgld_plan_buffers* plan,
+                                              const sgld_plan_geometry* geometry, void* stream) {
+  if (args == nullptr || geometry == nullptr)
+    return sgld::set_last_error(SGLD_ERR_INVALID_ARGUMENT, "decode args or geometry are NULL");
+  if (geometry->batch_capacity <= 0 || geometry->max_splits <= 0 || args->query_heads <= 0 ||
+      args->head_dim <= 0)
+    return sgld::set_last_error(SGLD_ERR_INVALID_ARGUMENT, "geometry fields must be positive");
+  const size_t slots = static_cast<size_t>(geometry->batch_capacity) * args->query_heads * geometry->max_splits;
+  const size_t partial_bytes = round_up(slots * args->head_dim * sizeof(float), 256);
+  const size_t lse_bytes = round_up(slots * sizeof(float), 256);
+  const size_t needed = kHeaderBytes + partial_bytes + lse_bytes;
+  if (needed > kScratchBytes) {
+    static thread_local char msg[256];
+    std::snprintf(msg, sizeof(msg),
+                  "this geometry needs %zu bytes of scratch; the allocation-free entry point holds at most "
+                  "%zu bytes (16 MiB) -- use sgld_decode_persistent with caller-owned scratch",
+                  needed, kScratchBytes);
+    return sgld::set_last_error(SGLD_ERR_INVALID_ARGUMENT, msg);
+  }
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
+    return sgld::set_last_error(SGLD_ERR_CUDA, "cudaGetDevice failed or device ordinal out of range");
+  unsigned char* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    if (g_scratch_addr[device] == nullptr) {
+      void* addr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+      if (e != cudaSuccess || addr == nullptr)
+        return sgld::set_last_error(SGLD_ERR_CUDA, "cudaGetSymbolAddress of the no-alloc scratch failed");
+      g_scratch_addr[device] = addr;
+    }
+    base = static_cast<unsigned char*>(g_scratch_addr[device]);
+  }
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Counter, exit ticket and status must start at zero; the rest is written before read.
+  if (cudaMemsetAsync(base, 0, 16, st) != cudaSuccess)
+    return sgld::set_last_error(SGLD_ERR_CUDA, "clearing the no-alloc scratch header failed");
+  sgld_decode_args a = *args;
+  a.counter = reinterpret_cast<int32_t*>(base);
+  if (a.status == nullptr) a.status = reinterpret_cast<int32_t*>(base + 8);
+  a.partial = reinterpret_cast<float*>(base + kHeaderBytes);
+  a.lse = reinterpret_cast<float*>(base + kHeaderBytes + partial_bytes);
+  return sgld_decode_persistent(&a, plan, geometry, stream);
+}

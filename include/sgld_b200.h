@@ -142,6 +142,22 @@ int sgld_merge_splits(const float* partial, const float* lse, const int32_t* cou
                       const int32_t* error, void* out, int32_t dtype, int32_t batch_capacity,
                       int32_t query_heads, int32_t head_dim, int32_t max_splits, void* stream);
 
+/*
+ * Allocation-free variant of sgld_decode_persistent for callers that cannot allocate
+ * device memory (no counterpart in the reference).  Hosts such as plugin interfaces that
+ * pass only input and output buffers, or servers that give all device memory to their
+ * KV-cache pool at start-up, have no place to put per-layer scratch.  Here the scratch
+ * (claim counter, status, fp32 partials and LSEs) lives in a 16 MiB device array owned by
+ * the library on every GPU that loads it; args->counter, ->partial and ->lse are ignored,
+ * args->status is used when non-NULL.  Geometries needing more than 16 MiB
+ * (Bcap*Hq*Smax*(D+1)*4 bytes plus 256) are rejected with SGLD_ERR_INVALID_ARGUMENT.
+ * Nothing is allocated.  The first call on a device looks up the array's device address
+ * (make it before any stream capture).  All calls share the array: calls whose GPU work
+ * overlaps race and must be serialised by the caller.
+ */
+int sgld_decode_persistent_noalloc(const sgld_decode_args* args, const sgld_plan_buffers* plan,
+                                   const sgld_plan_geometry* geometry, void* stream);
+
 /* Bytes of per-layer scratch (counter, partial, lse, status) for one decode
  * layer -- reference runtime/workspace.py:33-40 (LayerBuffers.allocate). */
 size_t sgld_layer_workspace_bytes(int32_t batch_capacity, int32_t query_heads, int32_t kv_heads,
