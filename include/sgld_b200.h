@@ -8,8 +8,9 @@
  *
  * Conventions
  *  - All pointers are DEVICE pointers unless stated otherwise; every buffer is
- *    owned by the caller.  No function allocates, frees or synchronises, so every
- *    call can be captured into a CUDA graph.
+ *    owned by the caller.  No function allocates, frees or synchronises;
+ *    sgld_plan_build, sgld_decode_persistent and sgld_merge_splits can be captured
+ *    into a CUDA graph.
  *  - `stream` is a cudaStream_t passed as void*; work is enqueued in stream order.
  *  - Return value: an sgld_status.  Non-zero means nothing was enqueued; the
  *    message is available from sgld_last_error() (thread-local).
