@@ -125,6 +125,18 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(power) if power else None}
 
 
+def traffic_ratio(workload):
+    """DRAM traffic per algorithmic byte of the decode kernel from the committed ncu summary
+    (profiles/decode_<workload>_traffic.md), or None when no capture exists for it."""
+    path = ROOT / "profiles" / f"decode_{workload.lower()}_traffic.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_per_algorithmic_byte"):
+            return float(line.split("=")[1])
+    return None
+
+
 def algorithmic_bytes(b, kv_heads_local, q_heads_local):
     """Σ L·Hkv·D·2(K,V)·elem + Q + O + index bytes (4·ΣL CSR, 4·Σceil(L/ps) paged)."""
     import torch
@@ -350,6 +362,8 @@ def run_ours(args):
     achieved = bytes_launch / (dec_ms * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
     clock = clocks.summary()
+    ratio = traffic_ratio(args.workload) if args.requests is None and world == 1 else None
+    traffic = int(ratio * bytes_launch) if ratio else None
 
     if rank == 0:
         cpu = None
@@ -370,12 +384,13 @@ def run_ours(args):
                        "heads_per_gpu": {"kv": hkv, "q": hq}, "workers": sms,
                        "l2": "not flushed: KV pool per GPU > 126 MB L2"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
-                         "peak_source": peak_kind, "kernel": "sgld decode_kernel (fused decode+merge)",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_source": peak_kind,
+                         "kernel": "decode_kernel timed with its PDL-chained merge_kernel (2% of the pair)",
                          "bytes_per_launch": bytes_launch, "kernel_us": round(dec_ms * 1000, 2)},
             "e2e": {"value": round(e2e_ms * 1000, 2), "unit": "us/layer", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,   # plan, decode, merge per step
             "clocks": clock,
         }
         if cpu is not None:
