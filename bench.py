@@ -241,8 +241,8 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    from sglang_decode.config import DecodeConfig
     from sglang_decode.runtime.engine import DecodeEngine
+    from sglang_decode.sharding import head_shard, shard_config
     from sglang_decode.workloads import baseline, generate, subset, update_plan
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -260,14 +260,10 @@ def run_ours(args):
     if args.requests is not None:
         b = subset(b, args.requests)
     c = b.config
-    if c.kv_heads % world:
-        raise SystemExit(f"{c.kv_heads} KV heads do not shard over {world} GPUs")
-    hkv = c.kv_heads // world
-    hq = c.query_heads // world
-    cfg = DecodeConfig(batch_capacity=c.batch_capacity, max_splits=c.max_splits,
-                       max_context=c.max_context, query_heads=hq, kv_heads=hkv,
-                       head_dim=c.head_dim, page_size=c.page_size, workers=sms)
-    data = generate(b, device=device, seed=17, kv_heads=hkv, head_offset=rank * hkv)
+    shard = head_shard(c, rank, world)      # KV heads [rank*Hkv/N, (rank+1)*Hkv/N) and their queries
+    hkv, hq = shard.kv_heads, shard.query_heads
+    cfg = shard_config(c, shard)
+    data = generate(b, device=device, seed=17, kv_heads=hkv, head_offset=shard.kv_offset)
     engine = DecodeEngine(cfg, device=device, dtype=b.dtype, force_mode=args.mode)
     update_plan(engine, b.lengths, b.splits)
     q, k, v, pages, indptr = data["q"], data["k"], data["v"], data["pages"], data["indptr"]
