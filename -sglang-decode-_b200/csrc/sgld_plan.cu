@@ -51,7 +51,7 @@ struct PlanShared {
   int32_t pk_count[kMaxBuckets];
   int32_t weight[kMaxRecords];
   unsigned long long keys[kMaxRecords];
-  int32_t loads[kMaxPlanWorkers];
+  int32_t loads[kMaxPlanWorkers + 4];   // serial LPT loads, or the parallel LPT's run starts
   int32_t tails[kMaxPlanWorkers];
 };
 
@@ -113,12 +113,108 @@ __device__ __forceinline__ int bucket_of(int w, int buckets) {
   return b;
 }
 
+// Exact LPT over the weight-sorted records (s.keys, heaviest first, lowest record id
+// first among equal weights), one worker per thread (W <= 1024).
+//
+// The reference assigns tasks one at a time to the least-loaded worker, lowest worker id
+// on ties (kernels/plan.py:120-135).  Within a run of k tasks of equal weight w this is
+// the same as handing out the k smallest "slots" (L_i + m*w, i), m >= 0, in that order.
+// With V0 = min L, L_i - V0 = q_i*w + rho_i (0 <= rho_i < w), slot (i, m) falls in round
+// q_i + m at offset rho_i, so slots are ordered by (round, rho_i, i): each round takes its
+// participants (q_i <= round) in (rho_i, i) order.  Rounds below max q_i need a block
+// scan of the participant flags; from max q_i on every worker takes part and worker i
+// gets task C + t*W + rank_i.  Every worker's tasks come in increasing order, so thread i
+// links its own list (head, next) exactly as the reference's append sequence leaves it.
+__device__ void static_lists_parallel(const PlanLaunch& a, PlanShared& s, int total, int G, int W) {
+  const sgld_plan_buffers& p = a.p;
+  const int tid = threadIdx.x;
+  const bool worker = tid < W;
+  int load = 0, tail = -1;
+  int* run_start = s.loads;          // [runs + 1] (the serial path's arrays are free here)
+  int* rank_of = s.tails;            // [W] position of worker i in (rho, i) order
+  int* pos = s.tails + 1024;         // [W] position among this round's participants
+  int* rho_s = s.tails + 2048;       // [W]
+  int* q_s = s.tails + 3072;         // [W]
+  // Run boundaries over the sorted positions (four contiguous positions per thread).
+  int flags = 0;
+  for (int k = 0; k < 4; ++k) {
+    const int idx = tid * 4 + k;
+    if (idx < total) {
+      const unsigned wk = static_cast<unsigned>(s.keys[idx] >> 32);
+      flags += (idx == 0 || wk != static_cast<unsigned>(s.keys[idx - 1] >> 32)) ? 1 : 0;
+    }
+  }
+  int runs = 0;
+  int rb = block_exclusive_scan(flags, s, runs);
+  for (int k = 0; k < 4; ++k) {
+    const int idx = tid * 4 + k;
+    if (idx < total && (idx == 0 || static_cast<unsigned>(s.keys[idx] >> 32) !=
+                                        static_cast<unsigned>(s.keys[idx - 1] >> 32)))
+      run_start[rb++] = idx;
+  }
+  if (tid == 0) run_start[runs] = total;
+  __syncthreads();
+  for (int r = 0; r < runs; ++r) {
+    const int rs = run_start[r], re = run_start[r + 1];
+    const int w = kIntMax - static_cast<int>(s.keys[rs] >> 32);
+    const int k = (re - rs) * G;                       // tasks in this run
+    const int v0 = block_reduce_min(worker ? load : kIntMax, s);
+    int q = 0, rho = 0;
+    if (worker) {
+      q = (load - v0) / w;
+      rho = (load - v0) - q * w;
+      q_s[tid] = q;
+      rho_s[tid] = rho;
+    }
+    const int qmax = block_reduce_max(worker ? q : 0, s);   // also publishes q_s / rho_s
+    int rank = 0;
+    if (worker) {
+      for (int j = 0; j < W; ++j) {
+        const int rj = rho_s[j];
+        rank += (rj < rho || (rj == rho && j < tid)) ? 1 : 0;
+      }
+      rank_of[rank] = tid;                             // rank -> worker
+    }
+    __syncthreads();
+    int assigned = 0, c = 0;
+    auto take = [&](int j) {                           // task j of the run goes to this worker
+      const int rec = static_cast<int>(s.keys[rs + j / G] & 0xffffffffu);
+      const int task = rec * G + j % G;
+      if (tail < 0) p.static_head[tid] = task;
+      else p.static_next[tail] = task;
+      p.static_next[task] = -1;
+      tail = task;
+      ++assigned;
+    };
+    for (int round = 0; round < qmax && c < k; ++round) {
+      // flag of the worker at sorted position tid, scanned in (rho, i) order
+      const int at = tid < W ? rank_of[tid] : 0;
+      const int flag = (tid < W && q_s[at] <= round) ? 1 : 0;
+      int n = 0;
+      const int before = block_exclusive_scan(flag, s, n);
+      if (flag) pos[at] = before;
+      __syncthreads();
+      if (worker && q <= round && c + pos[tid] < k) take(c + pos[tid]);
+      c += n;
+      __syncthreads();
+    }
+    if (worker) {
+      for (int j = c + rank; j < k; j += W) take(j);
+      load += assigned * w;
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PlanShared& s = *reinterpret_cast<PlanShared*>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const sgld_plan_buffers& p = a.p;
   const int bcap = a.bcap, G = a.groups, W = a.workers;
+  // The decode launched after this plan may start its prologue now (programmatic
+  // dependent launch); it waits for this grid's completion before reading the plan.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // ---------------------------------------------------------------- 1. count_scan
   const int active = *p.active;
@@ -319,6 +415,11 @@ __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
       __syncthreads();
     }
   }
+  if (W <= kThreads) {
+    static_lists_parallel(a, s, total, G, W);
+    return;
+  }
+  // More workers than threads: one warp runs the LPT task by task.
   if (warp != 0) return;
   for (int idx = 0; idx < total; ++idx) {
     const int rec = static_cast<int>(s.keys[idx] & 0xffffffffu);

@@ -54,7 +54,7 @@ def _random_case(rng):
         smax //= 2
     maxctx = rng.choice([64, 1000, 8192, 131072])
     hkv = rng.choice([1, 2, 4, 8])
-    workers = rng.choice([1, 5, 108, 148, 296])
+    workers = rng.choice([1, 5, 108, 148, 296, 1500])
     n = rng.randint(0, bcap)
     lengths = [rng.choice([0, 1, rng.randint(1, maxctx), maxctx]) for _ in range(n)]
     splits = [rng.randint(1, smax) for _ in range(n)]
