@@ -47,7 +47,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-triton"], default="ours")
     ap.add_argument("--workload", default="C3", choices=["C1", "C2", "C3", "C4"])
     ap.add_argument("--mode", type=int, default=-1, help="-1 AUTO, 0..4 force a mode")
     ap.add_argument("--requests", type=int, default=None,
@@ -397,10 +397,167 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_reference_triton(args):
+    """--impl reference-triton: the reference's own GPU path (Triton plan kernels, persistent
+    decode, merge) from the unmodified install in ``baseline/_ref``, timed on this GPU with the
+    same inputs and time boundary as ``run_ours`` (prepare + execute per step).  A comparator,
+    not the driver's reference arm; rank 0 only."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "sglang_decode" / "kernels" / "attention.py").is_file():
+        print(json.dumps({"impl": "reference-triton", "unavailable": "baseline/_ref is not installed"}))
+        return
+    # Inputs from this repo's seeded recipes (plain torch tensors; none of its kernels run) ...
+    from sglang_decode.workloads import baseline, generate
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    b = baseline(args.workload, workers=sms)
+    c = b.config
+    data = generate(b, device=device, seed=17)
+    # ... then the package name is handed over to the reference's install.
+    for name in [n for n in sys.modules if n == "sglang_decode" or n.startswith("sglang_decode.")]:
+        del sys.modules[name]
+    sys.path.insert(0, str(ref_root))
+    import sglang_decode as ref_pkg
+    if not Path(ref_pkg.__file__).resolve().is_relative_to(ref_root.resolve()):
+        raise SystemExit("reference-triton: imported the wrong sglang_decode")
+    from sglang_decode.config import DecodeConfig as RefConfig
+    from sglang_decode.runtime.engine import DecodeEngine as RefEngine
+
+    rc = RefConfig(batch_capacity=c.batch_capacity, max_splits=c.max_splits, max_context=c.max_context,
+                   query_heads=c.query_heads, kv_heads=c.kv_heads, head_dim=c.head_dim,
+                   page_size=c.page_size, workers=sms)
+    engine = RefEngine(rc, device=device, dtype=b.dtype, force_mode=args.mode)
+    p = engine.plan
+    n = len(b.lengths)
+    p.lengths.zero_()
+    p.splits.fill_(1)
+    p.active.fill_(n)
+    p.lengths[:n].copy_(torch.tensor(b.lengths, dtype=torch.int32))
+    p.splits[:n].copy_(torch.tensor(b.splits, dtype=torch.int32))
+    q, k, v, pages, indptr = data["q"], data["k"], data["v"], data["pages"], data["indptr"]
+
+    plan_note = "prepare + execute (the reference's Triton plan kernels, decode, merge)"
+    try:
+        engine.prepare()
+        torch.cuda.synchronize()
+        with_plan = True
+    except Exception as exc:            # the reference's plan kernel may not compile here
+        with_plan = False
+        first = str(exc).strip().splitlines()
+        reason = f"{type(exc).__name__}: {first[-1] if first else ''}"[:300]
+        plan_note = ("execute only (counter reset + Triton persistent_decode + merge_splits); its "
+                     "Triton plan kernels fail to build on this image (" + reason + "), so the plan "
+                     "tables come from the reference's CPU planning spec, uploaded before timing")
+        mode = _reference_host_tables(engine, b.lengths, b.splits, args.mode)
+        plan_note += f"; mode {mode}"
+
+    def step():
+        if with_plan:
+            engine.prepare()
+        return engine.execute(q, k, v, pages, indptr=indptr)
+
+    for _ in range(max(3, min(args.warmup, 5))):
+        step()
+    torch.cuda.synchronize()
+    out = step()
+    torch.cuda.synchronize()
+    finite = bool(torch.isfinite(out[:n].float()).all())
+    stream = torch.cuda.current_stream(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    one_ms = t0.elapsed_time(t1)
+    steps = max(3, min(args.steps, int(15000.0 / max(one_ms, 1e-3))))   # about 15 s at most
+    with ClockSampler(0) as clocks:
+        t0.record(stream)
+        for _ in range(steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+    step_ms = t0.elapsed_time(t1) / steps
+    bytes_launch = algorithmic_bytes(b, c.kv_heads, c.query_heads)
+    peak, peak_kind = measured_peak()
+    achieved = bytes_launch / (step_ms * 1e-3) / 1e9
+    print(json.dumps({
+        "impl": "reference-triton", "metric": METRIC, "value": round(step_ms * 1000, 2),
+        "unit": "us/layer", "n_gpus": 1, "steps": steps, "higher_is_better": False,
+        "dtype": {torch.float16: "f16", torch.bfloat16: "bf16"}[b.dtype], "data": "synthetic",
+        "config": {"workload": f"{b.name}: B={n} Hq={c.query_heads} Hkv={c.kv_heads} D={c.head_dim} "
+                               f"{'CSR' if b.csr else f'paged ps={c.page_size}'} sum(L)={sum(b.lengths)}",
+                   "mode": "AUTO" if args.mode < 0 else args.mode, "workers": sms},
+        "whole_step_hbm": {"achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                           "frac": round(achieved / peak, 4), "peak_source": peak_kind},
+        "boundary": plan_note, "finite_output": finite, "triton": __import__("triton").__version__,
+        "clocks": clocks.summary()}), flush=True)
+
+
+def _reference_host_tables(engine, lengths, splits, force_mode):
+    """Fill the reference engine's plan buffers from the reference's own CPU planning spec
+    (``planning/reference.py``: split_records, bucket_order, make_packs, greedy_static) in the
+    device layout its decode kernel reads (``kernels/plan.py`` semantics: R0/R1 identity order,
+    AUTO without rules = R1, width-1 packs for STATIC/D1, pack limit 4 for D4).  Returns the mode."""
+    import torch
+    from sglang_decode.planning.reference import bucket_order, greedy_static, make_packs, split_records
+
+    p, c = engine.plan, engine.config
+    records, counts, offsets = split_records(lengths, splits, c)
+    weights = [r.weight for r in records]
+    mode = force_mode if force_mode >= 0 else 1
+    if force_mode < 0 and weights and max(weights) == min(weights):
+        mode = 1
+    dev = p.device
+    t = lambda xs: torch.tensor(xs, dtype=torch.int32, device=dev)
+    n = len(lengths)
+    p.counts.zero_()
+    p.counts[:n].copy_(t(counts))
+    p.offsets.zero_()
+    p.offsets[:n + 1].copy_(t(offsets))
+    p.offsets[n + 1:].fill_(offsets[-1])
+    chunk = [((L + s - 1) // s + 31) // 32 * 32 for L, s in zip(lengths, splits)]
+    p.chunk.zero_()
+    p.chunk[:n].copy_(t(chunk))
+    p.record_count.fill_(len(records))
+    p.error.zero_()
+    p.mode.fill_(mode)
+    if records:
+        for name in ("request", "split", "begin", "end", "weight"):
+            getattr(p, name)[:len(records)].copy_(t([getattr(r, name) for r in records]))
+    order = list(range(len(records))) if mode in (0, 1) else bucket_order(records)
+    if order:
+        p.order[:len(order)].copy_(t(order))
+    packs = [] if mode in (0, 1) else make_packs(records, order, c.kv_heads, c.workers,
+                                                 4 if mode == 4 else 1)
+    p.num_packs.fill_(len(packs))
+    if packs:
+        p.pack_first[:len(packs)].copy_(t([f for f, _ in packs]))
+        p.pack_count[:len(packs)].copy_(t([k for _, k in packs]))
+    if mode == 2:
+        lists = greedy_static(records, c.kv_heads, c.workers)
+        heads, links = [-1] * c.workers, [-1] * c.task_capacity
+        for worker, tasks in enumerate(lists):
+            if tasks:
+                heads[worker] = tasks[0]
+            for left, right in zip(tasks, tasks[1:]):
+                links[left] = right
+        p.static_head.copy_(t(heads))
+        p.static_next.copy_(t(links))
+    torch.cuda.synchronize()
+    return mode
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "reference-triton":
+        run_reference_triton(args)
     else:
         run_ours(args)
 

@@ -101,6 +101,27 @@ def test_plan_baseline_shapes_match_oracle(name, force, cuda_device):
     assert got == want
 
 
+@pytest.mark.parametrize("workers", [7, 148, 1023, 1024, 1025])
+@pytest.mark.parametrize("maxctx", [8192, 1 << 21])
+def test_plan_static_lists_all_worker_and_weight_ranges(workers, maxctx, cuda_device):
+    """STATIC lists on the kernel's three LPT paths: weights up to 4096 (run table,
+    32-bit rank keys), heavier weights (contexts above 512K tokens: per-run max
+    reduction, 64-bit keys) and more than 1024 workers (serial LPT)."""
+    rng = random.Random(workers * 7 + maxctx)
+    bcap, smax, hkv = 64, 4, 4
+    for _ in range(3):
+        n = rng.randint(1, bcap)
+        lengths = [rng.choice([1, 33, 128, 129, rng.randint(1, maxctx), maxctx]) for _ in range(n)]
+        splits = [rng.randint(1, smax) for _ in range(n)]
+        cfg = DecodeConfig(batch_capacity=bcap, max_splits=smax, max_context=maxctx, query_heads=hkv * 2,
+                           kv_heads=hkv, head_dim=128, page_size=16, workers=workers)
+        g = geometry_of(cfg)
+        lb = lengths + [0] * (bcap - n)
+        sb = splits + [1] * (bcap - n)
+        want = oracle_tables_in_golden_format(P.device_tables(lb, sb, n, g, 2), g)
+        assert run_plan(cfg, lb, sb, n, 2, []) == want
+
+
 @pytest.mark.parametrize("shards", [1, 2, 4, 8])
 def test_plan_head_sharded_groups_match_oracle(shards, cuda_device):
     """Under KV-head sharding each GPU plans with groups = Hkv/N (C3)."""

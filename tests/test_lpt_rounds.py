@@ -1,6 +1,6 @@
 """The plan kernel's parallel LPT (equal-weight runs handed out round by round) equals the
 reference's one-task-at-a-time LPT.  A pure-Python model of the kernel's algorithm
-(sgld_plan.cu, static_lists_parallel) is compared with the oracle on random cases."""
+(sgld_plan.cu, static_lists_runs) is compared with the oracle on random cases."""
 import random
 
 import pytest
@@ -9,43 +9,75 @@ from oracle import planning as P
 
 
 def rounds_lpt(weights, groups, workers):
-    """Model of the kernel: runs of equal weight, rounds (q_i, rho_i), rank by (rho, i)."""
-    order = sorted(range(len(weights)), key=lambda i: (-weights[i], i))
-    loads = [0] * workers
-    heads, links, tails = [-1] * workers, {}, [-1] * workers
-    i = 0
-    while i < len(order):
-        j = i
-        while j < len(order) and weights[order[j]] == weights[order[i]]:
-            j += 1
-        w, run = weights[order[i]], order[i:j]
+    """Model of the kernel (sgld_plan.cu, static_lists_runs), step for step.
+
+    Runs come heaviest first; (q, rho) are taken against a zero baseline, rounds run from
+    min q to max q - 1; the
+    thread of rank t acts for worker rank_of[t]; pre-steady rounds hand out (round, rho, i)
+    slots; steady rounds give rank t tasks c + t + m*W with next[task(j)] = task(j + W)
+    written task-parallel; a worker's last task gets -1 at the end.  Every next[] entry
+    must be written exactly once (the kernel relies on it)."""
+    n = len(weights)
+    loads, tails, heads = [0] * workers, [-1] * workers, [-1] * workers
+    links, writes = {}, {}
+
+    def write(task, value):
+        writes[task] = writes.get(task, 0) + 1
+        links[task] = value
+
+    prev_w, consumed = 2**31 - 1, 0
+    while consumed < n:
+        w = max(x for x in weights if x < prev_w)
+        v0 = 0                                                   # any lower bound of the loads
+        run = [i for i in range(n) if weights[i] == w]           # ascending record ids
         k = len(run) * groups
-        v0 = min(loads)
         q = [(l - v0) // w for l in loads]
         rho = [(l - v0) % w for l in loads]
-        ranked = sorted(range(workers), key=lambda x: (rho[x], x))
-        assigned = [[] for _ in range(workers)]
-        c, rnd = 0, 0
+        rank_of = sorted(range(workers), key=lambda x: (rho[x], x))
+        task_of = lambda j: run[j // groups] * groups + j % groups
+        state = {}
+        for t, at in enumerate(rank_of):
+            state[t] = [at, q[at], tails[at], heads[at], 0]          # at, q, tail, head, assigned
+
+        def take(t, j):
+            st = state[t]
+            task = task_of(j)
+            if st[2] < 0:
+                st[3] = task
+            else:
+                write(st[2], task)
+            st[2] = task
+            st[4] += 1
+
+        c, rnd = 0, min(q)
         while rnd < max(q) and c < k:
-            part = [x for x in ranked if q[x] <= rnd]
-            for pos, x in enumerate(part):
+            part = [t for t in range(workers) if state[t][1] <= rnd]   # thread order = rank order
+            for pos, t in enumerate(part):
                 if c + pos < k:
-                    assigned[x].append(c + pos)
+                    take(t, c + pos)
             c += len(part)
             rnd += 1
-        for rank, x in enumerate(ranked):
-            assigned[x] += list(range(c + rank, k, workers))
-        for x in range(workers):
-            for jj in sorted(assigned[x]):
-                task = run[jj // groups] * groups + jj % groups
-                if tails[x] < 0:
-                    heads[x] = task
-                else:
-                    links[tails[x]] = task
-                links[task] = -1
-                tails[x] = task
-            loads[x] += len(assigned[x]) * w
-        i = j
+        for t in range(workers):
+            if c + t < k:
+                j0 = c + t
+                m = (k - 1 - j0) // workers
+                take(t, j0)
+                state[t][2] = task_of(j0 + m * workers)
+                state[t][4] += m
+        for j in range(c, k):
+            if j + workers < k:
+                write(task_of(j), task_of(j + workers))
+        for t in range(workers):
+            at, _, tail, head, assigned = state[t]
+            loads[at] += assigned * w
+            tails[at], heads[at] = tail, head
+        consumed += len(run)
+        prev_w = w
+    for x in range(workers):
+        if tails[x] >= 0:
+            write(tails[x], -1)
+    assert all(v == 1 for v in writes.values()), "a next[] entry was written twice"
+    assert len(writes) == n * groups, "a task has no next[] entry"
     return heads, links
 
 
