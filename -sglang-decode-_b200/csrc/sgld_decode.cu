@@ -67,8 +67,10 @@ struct Cfg {
   static constexpr bool kBig = D * NT >= 512;            // D=256 with a 16-row group
   static constexpr int kConsumerWarps = 4;
   // One warp's cp.async issue rate caps its bandwidth, so the copies are spread over
-  // as many producer warps as the register file allows next to the consumers.
-  static constexpr int kProducerWarps = kBig ? 2 : (NT == 2 ? 5 : 6);
+  // as many producer warps as the register file allows next to the consumers (16 warps
+  // at 128 registers for D <= 128 and a group of at most 8).  With tensor-map copies
+  // producer 0 works alone.
+  static constexpr int kProducerWarps = kBig ? 2 : (NT == 2 ? 5 : (D >= 256 ? 6 : 10));
   static constexpr int kProducerWarp0 = kConsumerWarps;
   static constexpr int kIndexerWarp = kProducerWarp0 + kProducerWarps;
   static constexpr int kSchedulerWarp = kIndexerWarp + 1;
@@ -393,6 +395,9 @@ struct Kernel {
   __device__ static void producer(const DecodeLaunch& a, unsigned char* smem, Misc& ms) {
     const int lane = threadIdx.x & 31;
     const int pw = (threadIdx.x >> 5) - C::kProducerWarp0;   // 0 .. P-1
+    // Tensor-map copies are issued by one thread: the other producer warps would only add
+    // barrier traffic (the barrier counts at set-up leave them out).
+    if (a.tma_kv && pw != 0) return;
     int* status = a.d.status;
     const T* kbase = static_cast<const T*>(a.d.k);
     const T* vbase = static_cast<const T*>(a.d.v);
@@ -707,8 +712,9 @@ struct Kernel {
     Misc& ms = *reinterpret_cast<Misc*>(smem + C::kOffMisc);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
+      const int producers = a.tma_kv ? 1 : C::kProducerWarps;   // warps that run the data ring
       for (int i = 0; i < C::kStages; ++i) {
-        mbar_init(&ms.full[i], 32 * C::kProducerWarps + 1);
+        mbar_init(&ms.full[i], 32 * producers + 1);
         mbar_init(&ms.empty[i], C::kConsumerWarps);
       }
       for (int i = 0; i < 2; ++i) {
@@ -721,7 +727,7 @@ struct Kernel {
       }
       for (int i = 0; i < C::kSD; ++i) {
         mbar_init(&ms.sfull[i], 1);
-        mbar_init(&ms.sempty[i], C::kProducerWarps);
+        mbar_init(&ms.sempty[i], producers);
       }
       mbar_init(&ms.join[0], C::kConsumerWarps);
       mbar_init(&ms.join[1], C::kConsumerWarps);
