@@ -217,6 +217,47 @@ def generate(b: Baseline, device="cuda", seed=17, kv_heads=None, head_offset=0):
     return dict(q=q, k=k, v=v, pages=pages, indptr=indptr)
 
 
+def graph_layer(b: Baseline, layer: int, device="cuda"):
+    """One layer of a graph Baseline (C5): its K/V pool and the full slot permutation.
+
+    Layer ``layer`` is seeded 17 + layer.  Request r's first L0_r tokens live in slots
+    perm[offset_r : offset_r + L0_r]; the token a request appends at replay step s
+    (s = 1, 2, ...) lives in slot perm[sum(L0) + (s - 1) * capacity + r].
+    Returns dict(k, v, perm, q) with q at the graph capacity.
+    """
+    c = b.config
+    gen = torch.Generator(device=device).manual_seed(17 + layer)
+    perm = torch.randperm(b.pool_tokens, generator=gen, device=device).int()
+    shape = (b.pool_tokens, c.kv_heads, c.head_dim)
+    k = _sharded_randn(shape, gen, device, b.dtype, c.kv_heads, 0)
+    v = _sharded_randn(shape, gen, device, b.dtype, c.kv_heads, 0)
+    q = torch.randn((c.batch_capacity, c.query_heads, c.head_dim), generator=gen, device=device, dtype=b.dtype)
+    return dict(k=k, v=v, perm=perm, q=q)
+
+
+def graph_step(b: Baseline, step: int, batch: int):
+    """Lengths and slot positions (into a layer's permutation) of replay step ``step``.
+
+    The batch is the first ``batch`` requests; each has appended ``step`` tokens.  The
+    positions are the same for every layer (each layer applies its own permutation).
+    Returns (lengths, positions) with positions a CPU int64 tensor of sum(lengths) entries.
+    """
+    cap = b.config.batch_capacity
+    total0 = sum(b.lengths)
+    if (step) * cap > b.pool_tokens - total0:
+        raise ValueError("the pool has no room for that many appended tokens")
+    lengths, parts, offset = [], [], 0
+    for r in range(batch):
+        n0 = b.lengths[r]
+        lengths.append(n0 + step)
+        parts.append(torch.arange(offset, offset + n0, dtype=torch.int64))
+        if step:
+            parts.append(total0 + r + cap * torch.arange(step, dtype=torch.int64))
+        offset += n0
+    positions = torch.cat(parts) if parts else torch.zeros(0, dtype=torch.int64)
+    return lengths, positions
+
+
 def _sharded_randn(shape, gen, device, dtype, hkv, head_offset, chunk_rows=1 << 16):
     """randn of the full [..., Hkv, D] pool, keeping heads [offset, offset+hkv) only.
 

@@ -48,7 +48,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference", "reference-triton"], default="ours")
-    ap.add_argument("--workload", default="C3", choices=["C1", "C2", "C3", "C4"])
+    ap.add_argument("--workload", default="C3", choices=["C1", "C2", "C3", "C4", "C5"])
     ap.add_argument("--mode", type=int, default=-1, help="-1 AUTO, 0..4 force a mode")
     ap.add_argument("--requests", type=int, default=None,
                     help="profile a prefix sub-workload (first N requests); not a bench line")
@@ -397,6 +397,116 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_graph(args):
+    """--workload C5: the Qwen2-7B-shaped step (28 layers, Hq=28, Hkv=4, group 7, bf16, CSR)
+    as one CUDA graph captured at capacity 128 and replayed over the shrinking batch sequence
+    128 -> 96 -> 64 -> 33 -> 1, each request appending one token per step (its slot taken
+    from the layer's own pool permutation).  One replay = the GPU plan build plus decode +
+    merge for all 28 layers.  value = µs per layer, averaged over the batch sequence; each
+    batch size is replayed ``--steps`` times on device-resident inputs (inputs change only
+    between batch sizes, outside the timed region)."""
+    import torch
+
+    from sglang_decode.runtime.engine import DecodeEngine, PlanKey
+    from sglang_decode.runtime.graph import DecodeGraph
+    from sglang_decode.workloads import baseline, graph_layer, graph_step, split_hints
+
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("--workload C5 runs on one GPU (its graph holds all 28 layers)")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    b = baseline("C5", workers=sms)
+    c = b.config
+    layers = [graph_layer(b, i, device=device) for i in range(b.layers)]
+    engine = DecodeEngine(c, device=device, dtype=b.dtype, layers=b.layers, force_mode=args.mode)
+    key = PlanKey("csr", "split_hints16", (c.query_heads, c.kv_heads))
+    graph = DecodeGraph(engine, [key] * b.layers, [(x["k"], x["v"]) for x in layers], csr=True,
+                        index_capacity=b.pool_tokens)
+    split = lambda lengths: split_hints(lengths, c.max_splits)
+
+    def feed(step, batch):
+        lengths, pos = graph_step(b, step, batch)
+        pos = pos.to(device)
+        graph.update([x["q"][:batch] for x in layers], [x["perm"][pos] for x in layers], lengths,
+                     split(lengths))
+        return lengths
+
+    feed(0, c.batch_capacity)
+    graph.capture(warmup=max(3, min(args.warmup, 5)))
+    stream = torch.cuda.current_stream(device)
+    per_batch, bytes_batch = {}, {}
+    elem = torch.finfo(b.dtype).bits // 8
+    with ClockSampler(0) as clocks:
+        for step, batch in enumerate(b.replay_batches):
+            lengths = feed(step, batch)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            t1.record(stream)
+            torch.cuda.synchronize()
+            per_batch[batch] = t0.elapsed_time(t1) / args.steps * 1000 / b.layers
+            bytes_batch[batch] = (sum(lengths) * c.kv_heads * c.head_dim * 2 * elem
+                                  + 2 * batch * c.query_heads * c.head_dim * elem + 4 * sum(lengths))
+            if engine.layers[0].status.item() != 0:
+                raise SystemExit("decode status word set during the C5 replay")
+    outs = graph.replay()
+    torch.cuda.synchronize()
+    if not all(torch.isfinite(o[:1].float()).all() for o in outs):
+        raise SystemExit("non-finite C5 output")
+    value = statistics.mean(per_batch.values())
+    peak, peak_kind = measured_peak()
+    big = b.replay_batches[0]
+    achieved = bytes_batch[big] / (per_batch[big] * 1e-6) / 1e9
+
+    # e2e: per batch size, update() from pinned host buffers + replay + read back all outputs.
+    host = [(x["q"].cpu().pin_memory(), x["perm"].cpu().pin_memory()) for x in layers]
+    h_out = [torch.empty_like(layer.output, device="cpu").pin_memory() for layer in engine.layers]
+    e2e_times, h2d, d2h = [], 0, 0
+    for step, batch in enumerate(b.replay_batches):
+        lengths, pos = graph_step(b, step, batch)
+        qs = [hq[:batch] for hq, _ in host]
+        idx = [hp[pos].pin_memory() for _, hp in host]
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.update(qs, idx, lengths, split(lengths))
+        outs = graph.replay()
+        for ho, o in zip(h_out, outs):
+            ho[:batch].copy_(o[:batch], non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_times.append(e0.elapsed_time(e1) * 1000 / b.layers)
+        h2d += sum(q.numel() * q.element_size() + i.numel() * 4 for q, i in zip(qs, idx)) + 8 * batch
+        d2h += sum(batch * c.query_heads * c.head_dim * elem for _ in outs)
+    n_steps = len(b.replay_batches)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "us/layer", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value * b.layers / 1000, 4),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"C5: {b.layers} layers Hq={c.query_heads} Hkv={c.kv_heads} D={c.head_dim} CSR "
+                               f"CUDA graph at capacity {c.batch_capacity}, replay {list(b.replay_batches)}",
+                   "mode": "AUTO" if args.mode < 0 else args.mode, "workers": sms,
+                   "us_per_layer_by_batch": {str(k): round(v, 2) for k, v in per_batch.items()},
+                   "step": "one graph replay (plan + 28 x decode + merge) per timed iteration",
+                   "l2": "not flushed: 16 GB of KV pools > 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_kind,
+                     "kernel": f"whole replay at batch {big} (plan + decode + merge per layer)",
+                     "bytes_per_launch": bytes_batch[big]},
+        "e2e": {"value": round(statistics.mean(e2e_times), 2), "unit": "us/layer",
+                "h2d_bytes_per_step": h2d // n_steps, "d2h_bytes_per_step": d2h // n_steps},
+        "gpu_launches": (1 + 2 * b.layers) * args.steps * n_steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference_triton(args):
     """--impl reference-triton: the reference's own GPU path (Triton plan kernels, persistent
     decode, merge) from the unmodified install in ``baseline/_ref``, timed on this GPU with the
@@ -558,6 +668,8 @@ def main():
         run_reference(args)
     elif args.impl == "reference-triton":
         run_reference_triton(args)
+    elif args.workload == "C5":
+        run_graph(args)
     else:
         run_ours(args)
 
