@@ -176,6 +176,8 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   const sgld_decode_args& d = *args;
   if (!d.q || !d.k || !d.v || !d.out || !d.pages || !d.counter || !d.partial || !d.lse || !d.status)
     return fail(SGLD_ERR_INVALID_ARGUMENT, "a tensor or scratch pointer is NULL");
+  if (!aligned16(d.partial))   // the epilogue and the merge move partial rows as float4
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "partial must be 16-byte aligned");
   if (d.dtype != SGLD_DTYPE_F16 && d.dtype != SGLD_DTYPE_BF16)
     return fail(SGLD_ERR_INVALID_ARGUMENT, "dtype must be fp16 or bf16");
   if (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256)
@@ -207,9 +209,12 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   a.fast_q = (aligned16(d.q) && d.q_stride[2] == 1 && d.q_stride[0] % 8 == 0 && d.q_stride[1] % 8 == 0) ? 1 : 0;
   // Paged KV by tensor-map TMA: a box of 32 tokens never crosses a page because stages
   // start 32-token aligned and 32 divides the page size.  Smaller pages stay on the
-  // multi-warp cp.async path, which measured faster than 8- or 16-row boxes.
+  // multi-warp cp.async path, which measured faster than 8- or 16-row boxes.  So do
+  // D <= 128 kernels with a group of at most 8: they carry 10 cp.async producer warps,
+  // which outrun a single thread issuing boxes (C4, page 64: 982 vs 1080 us).
   const int ps = d.page_size;
-  if (!csr && fast_kv && ps % 32 == 0 && d.kv_extent > 0 &&
+  const bool wide_cp_async = d.head_dim <= 128 && group <= 8;
+  if (!csr && fast_kv && ps % 32 == 0 && !wide_cp_async && d.kv_extent > 0 &&
       d.kv_extent < (int64_t{1} << 31) && !tma_disabled_by_env()) {
     const int box_rows = 32;
     if (encode_paged_map(&a.kmap, d.k, d.dtype, d.head_dim, d.kv_heads, ps, d.kv_extent, d.k_stride, box_rows) &&

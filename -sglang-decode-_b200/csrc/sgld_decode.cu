@@ -674,27 +674,37 @@ struct Kernel {
           red[(warp * C::kQRows + head) * C::kRedStride + d] = o[mt][nt][i];
         }
     if (!consumer_join(&ms.join[buf], (task_idx >> (C::kRedBufs == 2 ? 1 : 0)) & 1, a.d.status)) return false;
-    // 2. one pass: rescale to the global max, sum the warps, normalise, store
+    // 2. rescale every warp's state to the group max, sum the warps, normalise, store.  One
+    //    item is four consecutive dims of one head: the head's scale factors are computed
+    //    once per item and every warp's row is read as a float4 (rows are 16-byte aligned:
+    //    kRedStride is a multiple of 4).  Sums run over the warps in order, as one element
+    //    at a time would.
     const int64_t slot0 = (static_cast<int64_t>(h.request) * hq + h.group * gs) * smax + h.split;
-    for (int idx = ctid; idx < gs * D; idx += C::kConsumerThreads) {
-      const int head = idx / D, d = idx % D;
-      float mw[C::kConsumerWarps];
+    constexpr int D4 = D / 4;
+    for (int idx = ctid; idx < gs * D4; idx += C::kConsumerThreads) {
+      const int head = idx / D4, d = (idx - head * D4) * 4;
+      float sw[C::kConsumerWarps];
       float gm = -INFINITY;
 #pragma unroll
       for (int w = 0; w < C::kConsumerWarps; ++w) {
-        mw[w] = ms.m[buf][w][head];
-        gm = fmaxf(gm, mw[w]);
+        sw[w] = ms.m[buf][w][head];
+        gm = fmaxf(gm, sw[w]);
       }
-      float gl = 0.f, v = 0.f;
+      float gl = 0.f;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int w = 0; w < C::kConsumerWarps; ++w) {
-        const float sw = mw[w] == -INFINITY ? 0.f : ex2(mw[w] - gm);
-        gl += ms.l[buf][w][head] * sw;
-        v += red[(w * C::kQRows + head) * C::kRedStride + d] * sw;
+        sw[w] = sw[w] == -INFINITY ? 0.f : ex2(sw[w] - gm);
+        gl += ms.l[buf][w][head] * sw[w];
+        const float4 r = *reinterpret_cast<const float4*>(red + (w * C::kQRows + head) * C::kRedStride + d);
+        v.x += r.x * sw[w];
+        v.y += r.y * sw[w];
+        v.z += r.z * sw[w];
+        v.w += r.w * sw[w];
       }
-      const float res = v / gl;
+      const float4 res = make_float4(v.x / gl, v.y / gl, v.z / gl, v.w / gl);
       const int64_t slot = slot0 + static_cast<int64_t>(head) * smax;
-      a.d.partial[slot * D + d] = res;
+      *reinterpret_cast<float4*>(a.d.partial + slot * D + d) = res;   // 16-byte aligned (checked at entry)
       if (d == 0) a.d.lse[slot] = (gm + lg2(gl)) * kLn2;
     }
     if (C::kRedBufs == 1) {   // single reduction buffer: drain before the next task reuses it

@@ -115,7 +115,7 @@ typedef struct sgld_decode_args {
   float scale;          /* softmax scale (reference default head_dim^-0.5)                   */
   /* Layer scratch -- reference runtime/workspace.py:26-40 (LayerBuffers) */
   int32_t* counter;     /* [2]  claim counter + exit ticket; zero before, left zero after    */
-  float* partial;       /* [B, Hq, Smax, D] fp32 normalised split outputs                    */
+  float* partial;       /* [B, Hq, Smax, D] fp32 normalised split outputs, 16-byte aligned   */
   float* lse;           /* [B, Hq, Smax]    fp32 natural-log LSE per split                   */
   int32_t* status;      /* [1]  0 = ok; bounded in-kernel wait expired otherwise (sticky)    */
 } sgld_decode_args;

@@ -68,6 +68,10 @@ def test_host_checks_reject_bad_arguments_without_touching_a_gpu(lib):
     args.q = args.k = args.v = args.out = args.pages = 16
     args.counter = args.partial = args.lse = args.status = 16
     args.dtype, args.query_heads, args.kv_heads, args.head_dim, args.page_size = 1, 32, 8, 96, 16
+    args.partial = 20                                          # the epilogue and merge store float4 rows
+    assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 1
+    assert b"16-byte aligned" in lib.sgld_last_error()
+    args.partial = 16
     assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 2
     assert b"head dimensions" in lib.sgld_last_error()
     args.head_dim, args.query_heads = 128, 8 * 17
