@@ -50,6 +50,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference", "reference-triton"], default="ours")
     ap.add_argument("--workload", default="C3", choices=["C1", "C2", "C3", "C4", "C5"])
     ap.add_argument("--mode", type=int, default=-1, help="-1 AUTO, 0..4 force a mode")
+    ap.add_argument("--policy", default=None, help="validated AUTO policy JSON (rules for mode -1)")
     ap.add_argument("--requests", type=int, default=None,
                     help="profile a prefix sub-workload (first N requests); not a bench line")
     ap.add_argument("--e2e-steps", type=int, default=None)
@@ -264,7 +265,9 @@ def run_ours(args):
     hkv, hq = shard.kv_heads, shard.query_heads
     cfg = shard_config(c, shard)
     data = generate(b, device=device, seed=17, kv_heads=hkv, head_offset=shard.kv_offset)
-    engine = DecodeEngine(cfg, device=device, dtype=b.dtype, force_mode=args.mode)
+    from sglang_decode.planning.policy import load_policy
+    engine = DecodeEngine(cfg, device=device, dtype=b.dtype, force_mode=args.mode,
+                          rules=load_policy(args.policy))
     update_plan(engine, b.lengths, b.splits)
     q, k, v, pages, indptr = data["q"], data["k"], data["v"], data["pages"], data["indptr"]
 
@@ -377,6 +380,7 @@ def run_ours(args):
                                    f"D={c.head_dim} {'CSR' if b.csr else f'paged ps={c.page_size}'} "
                                    f"sum(L)={sum(b.lengths)}",
                        "mode": "AUTO" if args.mode < 0 else args.mode,
+                       "policy": Path(args.policy).name if args.policy else None,
                        "heads_per_gpu": {"kv": hkv, "q": hq}, "workers": sms,
                        "l2": "not flushed: KV pool per GPU > 126 MB L2"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
