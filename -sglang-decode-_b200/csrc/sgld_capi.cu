@@ -178,6 +178,8 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
     return fail(SGLD_ERR_INVALID_ARGUMENT, "a tensor or scratch pointer is NULL");
   if (!aligned16(d.partial))   // the epilogue and the merge move partial rows as float4
     return fail(SGLD_ERR_INVALID_ARGUMENT, "partial must be 16-byte aligned");
+  if (!(d.logit_cap >= 0.f) || d.logit_cap > 3.0e38f)   // rejects NaN, negatives and infinity
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "logit_cap must be a finite value >= 0 (0 disables it)");
   if (d.dtype != SGLD_DTYPE_F16 && d.dtype != SGLD_DTYPE_BF16)
     return fail(SGLD_ERR_INVALID_ARGUMENT, "dtype must be fp16 or bf16");
   if (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256)

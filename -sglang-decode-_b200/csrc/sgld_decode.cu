@@ -508,7 +508,13 @@ struct Kernel {
   __device__ static void consumer(const DecodeLaunch& a, unsigned char* smem, Misc& ms) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g8 = lane >> 2, t4 = lane & 3;
-    const float sc = a.d.scale * kLog2e;
+    // Scores go to the log2 domain.  With a soft cap (logit_cap > 0) the scaled score s
+    // becomes cap * tanh(s / cap) first; tanh comes from 1 - 2 / (2^(2x log2 e) + 1), exact at
+    // both saturations (2^big = inf gives 1, 2^-big = 0 gives -1).
+    const float cap = a.d.logit_cap;
+    const bool capped = cap > 0.f;
+    const float sc = capped ? a.d.scale : a.d.scale * kLog2e;
+    const float cap_log2e = cap * kLog2e, two_log2e_over_cap = capped ? 2.f * kLog2e / cap : 0.f;
     int* status = a.d.status;
 
     constexpr int KS = D / 16;   // k-steps of QK == m-tiles of O^T
@@ -579,7 +585,9 @@ struct Kernel {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int tok = g8 + (i >= 2 ? 8 : 0);
-            sv[i] = tok < valid ? (sa[nt][i] + sb[nt][i]) * sc : -INFINITY;
+            float x = (sa[nt][i] + sb[nt][i]) * sc;
+            if (capped) x = cap_log2e * (1.f - 2.f / (ex2(x * two_log2e_over_cap) + 1.f));
+            sv[i] = tok < valid ? x : -INFINITY;
           }
 #pragma unroll
           for (int jj = 0; jj < 2; ++jj) {

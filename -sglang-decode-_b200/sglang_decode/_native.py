@@ -40,7 +40,7 @@ class DecodeArgs(ctypes.Structure):
         ("v_stride", ctypes.c_int64 * 4), ("pt_stride", ctypes.c_int64 * 2),
         ("kv_extent", ctypes.c_int64),
         ("dtype", ctypes.c_int32), ("query_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
-        ("head_dim", ctypes.c_int32), ("page_size", ctypes.c_int32), ("scale", ctypes.c_float),
+        ("head_dim", ctypes.c_int32), ("page_size", ctypes.c_int32), ("scale", ctypes.c_float), ("logit_cap", ctypes.c_float),
         ("counter", ctypes.c_void_p), ("partial", ctypes.c_void_p), ("lse", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
     ]
@@ -50,7 +50,7 @@ DTYPE_F16, DTYPE_BF16 = 0, 1
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error"}
 EXPORTS = ("sgld_abi_version", "sgld_last_error", "sgld_layer_workspace_bytes", "sgld_plan_build",
            "sgld_decode_persistent", "sgld_merge_splits")
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 _lock = threading.Lock()
 _lib = None

@@ -2,11 +2,11 @@
 
 Source-compatible with the reference's ``integrations/sglang_backend.py:1-108``:
 the model-runner import patch selects this subclass; unsupported model geometry,
-logit caps, speculative modes, sliding windows and capacity overflow keep the
-original decode.  The decode itself runs on the B200 engine (one plan build per
+speculative modes, sliding windows and capacity overflow keep the original decode.  The decode itself runs on the B200 engine (one plan build per
 step, one fused decode launch per layer over SGLang's CSR kv_indptr/kv_indices).
-Difference from the reference: any integer GQA group 1..16 is eligible (Qwen2-7B's
-group of 7 included), so only groups above 16 fall back.
+Differences from the reference: any integer GQA group 1..16 is eligible (Qwen2-7B's
+group of 7 included), so only groups above 16 fall back; and layers with a logit soft
+cap (``layer.logit_cap > 0``) run on the engine with that cap instead of falling back.
 """
 import os
 
@@ -88,7 +88,7 @@ class ScheduledTritonBackend(TritonAttnBackend):
         if layer.layer_id == 0:
             self._prepared = False
         engine = self.scheduled
-        if (not self._eligible_step or layer.logit_cap > 0
+        if (not self._eligible_step
                 or layer.tp_q_head_num != engine.config.query_heads
                 or layer.tp_k_head_num != engine.config.kv_heads
                 or layer.qk_head_dim != engine.config.head_dim
@@ -111,5 +111,6 @@ class ScheduledTritonBackend(TritonAttnBackend):
         out = engine.execute(
             qbuf, forward_batch.token_to_kv_pool.get_key_buffer(layer.layer_id),
             forward_batch.token_to_kv_pool.get_value_buffer(layer.layer_id), meta.kv_indices,
-            layer=layer.layer_id, indptr=meta.kv_indptr, scale=layer.scaling)
+            layer=layer.layer_id, indptr=meta.kv_indptr, scale=layer.scaling,
+            logit_cap=max(0.0, float(layer.logit_cap or 0.0)))
         return out[:batch].view(batch, -1)

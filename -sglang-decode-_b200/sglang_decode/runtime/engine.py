@@ -3,7 +3,7 @@
 Same API and checks as the reference's ``runtime/engine.py:1-74``:
 ``DecodeEngine(config, device, dtype, layers, rules, force_mode)`` with
 ``prepare()`` (GPU plan build, once per compatible group per step) and
-``execute(q, k, v, pages, layer=0, *, indptr=None, scale=None)`` (paged
+``execute(q, k, v, pages, layer=0, *, indptr=None, scale=None, logit_cap=0.0)`` (paged
 ``[page, token, head, dim]`` or CSR ``[token, head, dim]`` KV, arbitrary strides).
 ``execute`` enqueues the sm_100a persistent decode kernel and the split merge (a
 programmatic dependent launch that overlaps the decode's tail); the claim counter is
@@ -48,11 +48,13 @@ class DecodeEngine:
         """Call once per compatible group per step, including on every graph replay."""
         build_plan(self.plan, self.force_mode)
 
-    def execute(self, q, k, v, pages, layer=0, *, indptr=None, scale=None):
+    def execute(self, q, k, v, pages, layer=0, *, indptr=None, scale=None, logit_cap=0.0):
         """KV layout: [pages,page_size,kv_heads,D], or CSR [tokens,kv_heads,D].
 
         Metadata and Q/KV must be ready on the current CUDA stream. Fixed buffers
         are reused; consumers must finish before reusing this execution instance.
+        ``logit_cap`` > 0 soft-caps the scaled scores, s -> cap * tanh(s / cap), as SGLang
+        does for models such as Gemma-2 (an addition: the reference has no capped path).
         """
         c, p, out = self.config, self.plan, self.layers[layer]
         if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
@@ -99,6 +101,10 @@ class DecodeEngine:
         a.dtype = _DTYPES[q.dtype]
         a.query_heads, a.kv_heads, a.head_dim = c.query_heads, c.kv_heads, c.head_dim
         a.scale = c.head_dim ** -0.5 if scale is None else float(scale)
+        cap = float(logit_cap or 0.0)
+        if not cap >= 0.0 or cap == float("inf"):
+            raise ValueError("logit_cap must be a finite value >= 0 (0 disables it)")
+        a.logit_cap = cap
         a.counter, a.partial, a.lse = out.counter.data_ptr(), out.partial.data_ptr(), out.lse.data_ptr()
         a.status = out.status.data_ptr()
         stream = torch.cuda.current_stream(p.device).cuda_stream

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define SGLD_ABI_VERSION 3
+#define SGLD_ABI_VERSION 4
 
 typedef enum sgld_status {
   SGLD_OK = 0,
@@ -113,6 +113,10 @@ typedef struct sgld_decode_args {
   int32_t head_dim;     /* 64, 128 or 256                                                    */
   int32_t page_size;    /* 1 for CSR                                                         */
   float scale;          /* softmax scale (reference default head_dim^-0.5)                   */
+  float logit_cap;      /* > 0: each scaled score s becomes logit_cap * tanh(s / logit_cap)
+                           before the softmax (SGLang's soft cap, upstream
+                           decode_attention.py:127-128); 0 disables it; not in the
+                           reference's own kernel (its adapter falls back)              */
   /* Layer scratch -- reference runtime/workspace.py:26-40 (LayerBuffers) */
   int32_t* counter;     /* [2]  claim counter + exit ticket; zero before, left zero after    */
   float* partial;       /* [B, Hq, Smax, D] fp32 normalised split outputs, 16-byte aligned   */

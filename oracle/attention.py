@@ -29,9 +29,14 @@ def _group(q: np.ndarray, k: np.ndarray) -> int:
     return hq // hkv
 
 
-def _attend(qr: np.ndarray, key: np.ndarray, value: np.ndarray, group: int, scale: float):
+def _attend(qr: np.ndarray, key: np.ndarray, value: np.ndarray, group: int, scale: float,
+            logit_cap: float = 0.0):
     """One request: qr [Hq, D], key/value [T, Hkv, D] (any float dtype, upcast here)
-    -> [Hq, D] FP32 softmax attention, one KV head at a time (strided BLAS views)."""
+    -> [Hq, D] FP32 softmax attention, one KV head at a time (strided BLAS views).
+
+    ``logit_cap > 0`` soft-caps the scaled scores, s -> cap * tanh(s / cap), before the
+    softmax (SGLang's decode, vendored in the reference at
+    ``third_party/sglang/decode_attention.py:124-128``)."""
     hkv, d = key.shape[1], qr.shape[-1]
     q3 = qr.reshape(hkv, group, d).astype(np.float32)
     key = key.astype(np.float32, copy=False)
@@ -39,6 +44,8 @@ def _attend(qr: np.ndarray, key: np.ndarray, value: np.ndarray, group: int, scal
     out = np.empty((hkv, group, d), dtype=np.float32)
     for h in range(hkv):
         score = (q3[h] @ key[:, h, :].T) * np.float32(scale)                 # [G, T]
+        if logit_cap > 0:
+            score = np.float32(logit_cap) * np.tanh(score / np.float32(logit_cap))
         score -= score.max(axis=-1, keepdims=True)
         prob = np.exp(score)
         prob /= prob.sum(axis=-1, keepdims=True)
@@ -46,7 +53,7 @@ def _attend(qr: np.ndarray, key: np.ndarray, value: np.ndarray, group: int, scal
     return out.reshape(qr.shape)
 
 
-def paged_attention(q, k, v, pages, lengths, page_size, scale=None):
+def paged_attention(q, k, v, pages, lengths, page_size, scale=None, logit_cap=0.0):
     """FP32 paged decode oracle (reference/attention.py:5-18).
 
     q [Bcap, Hq, D]; k, v [P, page_size, Hkv, D]; pages [Bcap, max_pages] int.
@@ -60,11 +67,11 @@ def paged_attention(q, k, v, pages, lengths, page_size, scale=None):
         token = np.arange(length)
         physical = np.asarray(pages[r])[token // page_size].astype(np.int64)
         inner = token % page_size
-        out[r] = _attend(q[r], k[physical, inner], v[physical, inner], group, scale)
+        out[r] = _attend(q[r], k[physical, inner], v[physical, inner], group, scale, logit_cap)
     return out
 
 
-def csr_attention(q, k, v, indptr, indices, lengths=None, scale=None):
+def csr_attention(q, k, v, indptr, indices, lengths=None, scale=None, logit_cap=0.0):
     """FP32 CSR decode oracle: token t of request r lives at row indices[indptr[r] + t].
 
     k, v [N, Hkv, D].  This is the page_size=1 path the reference's engine takes when
@@ -79,7 +86,7 @@ def csr_attention(q, k, v, indptr, indices, lengths=None, scale=None):
         if length == 0:
             continue
         rows = np.asarray(indices[int(indptr[r]):int(indptr[r]) + length]).astype(np.int64)
-        out[r] = _attend(q[r], k[rows], v[rows], group, scale)
+        out[r] = _attend(q[r], k[rows], v[rows], group, scale, logit_cap)
     return out
 
 

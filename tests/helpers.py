@@ -72,13 +72,14 @@ def f32(t):
     return t.detach().float().cpu().numpy()
 
 
-def oracle_paged(q, k, v, pages, lengths, page_size, scale=None):
-    return A.paged_attention(f32(q), f32(k), f32(v), pages.cpu().numpy(), lengths, page_size, scale)
+def oracle_paged(q, k, v, pages, lengths, page_size, scale=None, logit_cap=0.0):
+    return A.paged_attention(f32(q), f32(k), f32(v), pages.cpu().numpy(), lengths, page_size, scale,
+                             logit_cap)
 
 
-def oracle_csr(q, k, v, indptr, indices, lengths, scale=None):
+def oracle_csr(q, k, v, indptr, indices, lengths, scale=None, logit_cap=0.0):
     return A.csr_attention(f32(q), f32(k), f32(v), indptr.cpu().numpy(), indices.cpu().numpy(),
-                           lengths, scale)
+                           lengths, scale, logit_cap)
 
 
 def assert_within_tolerance(actual, expected, n, max_abs=2e-2, mean_abs=2e-3):

@@ -25,14 +25,14 @@ MIXED = [0, 1, 17, 33, 257, 513]
 B = [256] * 24 + [1536] * 4 + [16384] * 4
 
 
-def run(engine, inputs, lengths, splits=None, indptr=None, layer=0, scale=None):
+def run(engine, inputs, lengths, splits=None, indptr=None, layer=0, scale=None, logit_cap=0.0):
     update_plan(engine, lengths, splits)
     lb = engine.layers[layer]
     lb.partial.fill_(float("nan"))
     lb.lse.fill_(float("nan"))
     engine.prepare()
     q, k, v, pages = inputs
-    out = engine.execute(q, k, v, pages, layer=layer, indptr=indptr, scale=scale)
+    out = engine.execute(q, k, v, pages, layer=layer, indptr=indptr, scale=scale, logit_cap=logit_cap)
     torch.cuda.synchronize()
     assert lb.status.item() == 0, "bounded in-kernel wait expired"
     assert engine.counters.eq(0).all(), "claim counter / exit ticket not left at zero"
@@ -113,6 +113,48 @@ def test_csr_group_sizes_and_head_dims(dtype, group, head_dim, mode, cuda_device
     out = run(engine, (q, k, v, idx), lengths, indptr=indptr)
     expected = oracle_csr(q, k, v, indptr, idx, lengths)
     assert_within_tolerance(out, expected, len(lengths))
+
+
+@pytest.mark.parametrize("cap", [2.0, 20.0, 50.0])
+@pytest.mark.parametrize("layout", ["csr_g8", "csr_g7", "paged64_g4", "paged16_g16_d256"])
+def test_logit_soft_cap_matches_oracle_in_every_mode(cap, layout, cuda_device):
+    """SGLang's soft cap (s -> cap * tanh(s / cap)); Q scaled up so that the cap bites."""
+    lengths = [1, 65, 300, 0, 1000, 129, 700]
+    group, hkv, d = {"csr_g8": (8, 2, 128), "csr_g7": (7, 2, 128), "paged64_g4": (4, 4, 128),
+                     "paged16_g16_d256": (16, 1, 256)}[layout]
+    ps = {"paged64_g4": 64, "paged16_g16_d256": 16}.get(layout, 1)
+    c = DecodeConfig(batch_capacity=8, max_splits=8, max_context=1024, query_heads=hkv * group,
+                     kv_heads=hkv, head_dim=d, page_size=ps, workers=37)
+    if ps == 1:
+        q, k, v, idx, indptr = (t.cuda() for t in make_csr_inputs(c, lengths, device="cpu", pool=4000))
+        inputs = (4.0 * q, k, v, idx)
+        expected = oracle_csr(4.0 * q, k, v, indptr, idx, lengths, logit_cap=cap)
+        plain = oracle_csr(4.0 * q, k, v, indptr, idx, lengths)
+    else:
+        indptr = None
+        q, k, v, pages = (t.cuda() for t in make_inputs(c, lengths, device="cpu"))
+        inputs = (4.0 * q, k, v, pages)
+        expected = oracle_paged(4.0 * q, k, v, pages, lengths, ps, logit_cap=cap)
+        plain = oracle_paged(4.0 * q, k, v, pages, lengths, ps)
+    assert np.abs(expected - plain).max() > 1e-2, "the cap must change the result in this case"
+    outs = []
+    for mode in (Mode.R0, Mode.R1, Mode.STATIC, Mode.D1, Mode.D4):
+        out = run(DecodeEngine(c, force_mode=mode), inputs, lengths, indptr=indptr, logit_cap=cap)
+        assert_within_tolerance(out, expected, len(lengths))
+        outs.append(out.clone())
+    assert all(torch.equal(outs[0], o) for o in outs[1:]), "every dispatch mode gives identical outputs"
+
+
+def test_logit_cap_must_be_finite_and_non_negative(cuda_device):
+    c = DecodeConfig(batch_capacity=2, max_splits=2, max_context=64, query_heads=8, kv_heads=2,
+                     head_dim=128, page_size=1, workers=4)
+    q, k, v, idx, indptr = (t.cuda() for t in make_csr_inputs(c, [10, 20], device="cpu", pool=64))
+    engine = DecodeEngine(c)
+    update_plan(engine, [10, 20])
+    engine.prepare()
+    for bad in (-1.0, float("nan"), float("inf")):
+        with pytest.raises(ValueError):
+            engine.execute(q, k, v, idx, indptr=indptr, logit_cap=bad)
 
 
 @pytest.mark.parametrize("page_size", [1, 8, 16, 64])

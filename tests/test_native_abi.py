@@ -72,6 +72,11 @@ def test_host_checks_reject_bad_arguments_without_touching_a_gpu(lib):
     assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 1
     assert b"16-byte aligned" in lib.sgld_last_error()
     args.partial = 16
+    for bad in (-1.0, float("nan"), float("inf")):             # the soft cap must be finite and >= 0
+        args.logit_cap = bad
+        assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 1
+        assert b"logit_cap" in lib.sgld_last_error()
+    args.logit_cap = 0.0
     assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 2
     assert b"head dimensions" in lib.sgld_last_error()
     args.head_dim, args.query_heads = 128, 8 * 17
@@ -91,7 +96,7 @@ int main(void) {
   printf("sgld_decode_args %zu\n", sizeof(sgld_decode_args));
   F(sgld_plan_geometry, workers) F(sgld_plan_buffers, static_next)
   F(sgld_decode_args, q_stride) F(sgld_decode_args, kv_extent) F(sgld_decode_args, dtype)
-  F(sgld_decode_args, scale) F(sgld_decode_args, counter) F(sgld_decode_args, partial)
+  F(sgld_decode_args, scale) F(sgld_decode_args, logit_cap) F(sgld_decode_args, counter) F(sgld_decode_args, partial)
   F(sgld_decode_args, lse) F(sgld_decode_args, status)
   return 0;
 }
@@ -112,6 +117,6 @@ def test_ctypes_structs_match_the_c_header(tmp_path):
         "sgld_plan_geometry.workers": _native.PlanGeometry.workers.offset,
         "sgld_plan_buffers.static_next": _native.PlanBuffersC.static_next.offset,
     }
-    for field in ("q_stride", "kv_extent", "dtype", "scale", "counter", "partial", "lse", "status"):
+    for field in ("q_stride", "kv_extent", "dtype", "scale", "logit_cap", "counter", "partial", "lse", "status"):
         want[f"sgld_decode_args.{field}"] = getattr(_native.DecodeArgs, field).offset
     assert {k: int(v) for k, v in got.items()} == want

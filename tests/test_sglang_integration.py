@@ -119,7 +119,7 @@ def _oracle(backend, runner, fb, layer, q):
                            pool.k[layer.layer_id].float().cpu().numpy(),
                            pool.v[layer.layer_id].float().cpu().numpy(),
                            meta.kv_indptr.cpu().numpy(), meta.kv_indices.cpu().numpy(), lengths,
-                           layer.scaling)
+                           layer.scaling, logit_cap=layer.logit_cap)
 
 
 def _check(got, want):
@@ -173,8 +173,7 @@ def test_adapter_rebuilds_the_plan_per_layer_when_reuse_is_off(adapter, monkeypa
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("case", ["logit_cap", "sliding_window", "prefill", "over_capacity", "disabled",
-                                  "spec_info"])
+@pytest.mark.parametrize("case", ["sliding_window", "prefill", "over_capacity", "disabled", "spec_info"])
 def test_adapter_falls_back_to_the_original_decode(adapter, monkeypatch, case, cuda_device):
     if case == "over_capacity":
         monkeypatch.setenv("DECODE_BATCH_CAPACITY", "2")
@@ -187,8 +186,7 @@ def test_adapter_falls_back_to_the_original_decode(adapter, monkeypatch, case, c
     if case == "spec_info":
         fb.spec_info = object()
     backend.init_forward_metadata(fb)
-    layer = F.FakeLayer.make(0, 28, 4, 128, logit_cap=30.0 if case == "logit_cap" else 0.0,
-                             sliding_window_size=512 if case == "sliding_window" else -1)
+    layer = F.FakeLayer.make(0, 28, 4, 128, sliding_window_size=512 if case == "sliding_window" else -1)
     q = torch.randn(3, 28 * 128, device="cuda", dtype=torch.bfloat16)
     kv = torch.randn(3, 4, 128, device="cuda", dtype=torch.bfloat16)
     out = backend.forward_decode(q, kv, kv, layer, fb)
@@ -225,3 +223,23 @@ def test_adapter_cuda_graph_hooks_take_upstream_positional_arguments(adapter, cu
                                                     int(fb.seq_lens.sum()), None, F.FakeMode(True), object(),
                                                     fb.seq_lens.cpu())
     assert not backend._eligible_step
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cap", [5.0, 30.0, 50.0])
+def test_adapter_runs_soft_capped_layers_on_the_engine(adapter, cap, cuda_device):
+    """Gemma-2-style soft cap: the reference's adapter falls back; this one decodes with the cap."""
+    runner = _runner(32, 4, layers=1)
+    backend = adapter.ScheduledTritonBackend(runner)
+    fb = _batch(runner, [17, 300, 1500, 4000])
+    backend.init_forward_metadata(fb)
+    layer = F.FakeLayer.make(0, 32, 4, 128, logit_cap=cap)
+    g = torch.Generator(device="cuda").manual_seed(int(cap))
+    q = 3.0 * torch.randn(4, 32 * 128, generator=g, device="cuda", dtype=torch.bfloat16)   # large scores
+    kv = torch.randn(4, 4, 128, generator=g, device="cuda", dtype=torch.bfloat16)
+    out = backend.forward_decode(q, kv, kv, layer, fb)
+    torch.cuda.synchronize()
+    assert backend.fallback_calls == 0
+    _check(out, _oracle(backend, runner, fb, layer, q))
+    uncapped = _oracle(backend, runner, fb, F.FakeLayer.make(0, 32, 4, 128), q)
+    assert np.abs(_oracle(backend, runner, fb, layer, q) - uncapped).max() > 1e-3   # the cap matters here
