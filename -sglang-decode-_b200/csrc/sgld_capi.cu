@@ -180,10 +180,16 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
     return fail(SGLD_ERR_INVALID_ARGUMENT, "partial must be 16-byte aligned");
   if (!(d.logit_cap >= 0.f) || d.logit_cap > 3.0e38f)   // rejects NaN, negatives and infinity
     return fail(SGLD_ERR_INVALID_ARGUMENT, "logit_cap must be a finite value >= 0 (0 disables it)");
+  if (!(d.k_scale >= 0.f) || d.k_scale > 3.0e38f || !(d.v_scale >= 0.f) || d.v_scale > 3.0e38f)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "k_scale / v_scale must be finite values >= 0 (0 reads as 1)");
+  const bool kv_fp8 = d.kv_dtype == SGLD_DTYPE_E4M3;
+  if (!kv_fp8 && d.kv_dtype != d.dtype)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "kv_dtype must equal dtype or be SGLD_DTYPE_E4M3");
   if (d.dtype != SGLD_DTYPE_F16 && d.dtype != SGLD_DTYPE_BF16)
     return fail(SGLD_ERR_INVALID_ARGUMENT, "dtype must be fp16 or bf16");
   if (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256)
     return fail(SGLD_ERR_UNSUPPORTED, "supported head dimensions: 64, 128, 256");
+  if (kv_fp8 && d.head_dim != 128) return fail(SGLD_ERR_UNSUPPORTED, "fp8 K/V: head_dim 128 only");
   if (d.kv_heads <= 0 || d.query_heads <= 0 || d.query_heads % d.kv_heads)
     return fail(SGLD_ERR_INVALID_ARGUMENT, "query heads must be a positive multiple of KV heads");
   const int group = d.query_heads / d.kv_heads;
@@ -205,8 +211,14 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   a.group_size = group;
   a.csr = csr ? 1 : 0;
   if (csr) a.d.k_stride[1] = 0, a.d.v_stride[1] = 0;
+  // 16-byte copies need 16-byte aligned rows: strides in whole 16-byte chunks of elements.
+  const int64_t per_chunk = kv_fp8 ? 16 : 8;
   bool fast_kv = aligned16(d.k) && aligned16(d.v) && d.k_stride[3] == 1 && d.v_stride[3] == 1;
-  for (int i = 0; i < 3; ++i) fast_kv = fast_kv && (a.d.k_stride[i] % 8 == 0) && (a.d.v_stride[i] % 8 == 0);
+  for (int i = 0; i < 3; ++i)
+    fast_kv = fast_kv && (a.d.k_stride[i] % per_chunk == 0) && (a.d.v_stride[i] % per_chunk == 0);
+  a.kv_fp8 = kv_fp8 ? 1 : 0;
+  if (a.d.k_scale == 0.f) a.d.k_scale = 1.f;
+  if (a.d.v_scale == 0.f) a.d.v_scale = 1.f;
   a.fast_kv = fast_kv ? 1 : 0;
   a.fast_q = (aligned16(d.q) && d.q_stride[2] == 1 && d.q_stride[0] % 8 == 0 && d.q_stride[1] % 8 == 0) ? 1 : 0;
   // Paged KV by tensor-map TMA: a box of 32 tokens never crosses a page because stages
@@ -216,7 +228,7 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   // which outrun a single thread issuing boxes (C4, page 64: 982 vs 1080 us).
   const int ps = d.page_size;
   const bool wide_cp_async = d.head_dim <= 128 && group <= 8;
-  if (!csr && fast_kv && ps % 32 == 0 && !wide_cp_async && d.kv_extent > 0 &&
+  if (!csr && !kv_fp8 && fast_kv && ps % 32 == 0 && !wide_cp_async && d.kv_extent > 0 &&
       d.kv_extent < (int64_t{1} << 31) && !tma_disabled_by_env()) {
     const int box_rows = 32;
     if (encode_paged_map(&a.kmap, d.k, d.dtype, d.head_dim, d.kv_heads, ps, d.kv_extent, d.k_stride, box_rows) &&

@@ -39,6 +39,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 #include "sgld_internal.cuh"
 #include "sgld_ptx.cuh"
 
@@ -62,7 +64,7 @@ struct TaskDesc {
   int request, split, group, begin, end, count_r, base, valid;
 };
 
-template <int D, int NT>
+template <int D, int NT, bool F8 = false>
 struct Cfg {
   static constexpr bool kBig = D * NT >= 512;            // D=256 with a 16-row group
   static constexpr int kConsumerWarps = 4;
@@ -70,7 +72,9 @@ struct Cfg {
   // as many producer warps as the register file allows next to the consumers (16 warps
   // at 128 registers for D <= 128 and a group of at most 8).  With tensor-map copies
   // producer 0 works alone.
-  static constexpr int kProducerWarps = kBig ? 2 : (NT == 2 ? 5 : (D >= 256 ? 6 : 10));
+  // fp8 stages carry half the bytes; its 16-row-group kernel keeps 4 producers so the
+  // widening consumers fit in registers.
+  static constexpr int kProducerWarps = kBig ? 2 : (NT == 2 ? (F8 ? 4 : 5) : (D >= 256 ? 6 : 10));
   static constexpr int kProducerWarp0 = kConsumerWarps;
   static constexpr int kIndexerWarp = kProducerWarp0 + kProducerWarps;
   static constexpr int kSchedulerWarp = kIndexerWarp + 1;
@@ -78,13 +82,16 @@ struct Cfg {
   static constexpr int kThreads = kWarps * 32;
   static constexpr int kConsumerThreads = kConsumerWarps * 32;
   static constexpr int kTS = 64;                         // tokens per stage
-  static constexpr int kRowBytes = D * 2;
-  static constexpr int kChunks = D / 8;                  // 16-byte chunks per row
+  static constexpr int kKVBytes = F8 ? 1 : 2;            // bytes per K/V element (e4m3 or 16-bit)
+  static constexpr int kRowBytes = D * kKVBytes;
+  static constexpr int kChunks = kRowBytes / 16;         // 16-byte chunks per K/V row
+  static constexpr int kEPC = 16 / kKVBytes;             // K/V elements per 16-byte chunk
+  static constexpr int kQChunks = D / 8;                 // Q is 16-bit in shared memory
   static constexpr int kTPI = (32 / kChunks) > 0 ? 32 / kChunks : 1;  // tokens per warp copy
   static constexpr int kTileBytes = kTS * kRowBytes;
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kQRows = NT * 8;
-  static constexpr int kQBytes = kQRows * kRowBytes;
+  static constexpr int kQBytes = kQRows * D * 2;
   static constexpr int kRedStride = D + 4;               // floats; padding avoids bank conflicts
   static constexpr int kRedOne = kConsumerWarps * kQRows * kRedStride * 4;
   static constexpr int kTaskQ = 4;
@@ -93,21 +100,26 @@ struct Cfg {
   static constexpr int kSDEntry = kTS * 24;              // koff, voff (int64), page, row (int32)
   static constexpr int kSDBytes = kSD * kSDEntry;
   static constexpr int kMiscBytes = 4096;
-  static constexpr int kFixed1 = 2 * kQBytes + kSDBytes + kMiscBytes;
+  // fp8 K/V: each consumer warp widens its 16 rows of K and V to f16 here before the MMAs.
+  static constexpr int kScrTile = F8 ? 16 * D * 2 : 0;
+  static constexpr int kScratchBytes = 2 * kConsumerWarps * kScrTile;
+  static constexpr int kFixed1 = 2 * kQBytes + kSDBytes + kMiscBytes + kScratchBytes;
   static constexpr int kRedBufs = (kFixed1 + 2 * kRedOne + 3 * kStageBytes <= kSmemBudget) ? 2 : 1;
   static constexpr int kFixed = kFixed1 + kRedBufs * kRedOne;
   static constexpr int kStagesRaw = (kSmemBudget - kFixed) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static_assert(kStages >= 2, "shared memory budget too small");
   // Offsets from the 1024-byte aligned base (tiles first: they need the alignment).
-  static constexpr int kOffQ = kStages * kStageBytes;
+  static constexpr int kOffScratch = kStages * kStageBytes;
+  static constexpr int kOffQ = kOffScratch + kScratchBytes;
   static constexpr int kOffRed = kOffQ + 2 * kQBytes;
   static constexpr int kOffSD = kOffRed + kRedBufs * kRedOne;
   static constexpr int kOffMisc = kOffSD + kSDBytes;
   static constexpr int kSmemUsed = kOffMisc + kMiscBytes;
   static constexpr int kSmemBytes = kSmemUsed + 1024;    // launch size including alignment slack
   static_assert(kSmemUsed <= kSmemBudget, "shared memory budget exceeded");
-  static_assert(kTileBytes % 1024 == 0 && kQBytes % 1024 == 0, "tiles must keep 1024-byte alignment");
+  static_assert(kTileBytes % 1024 == 0 && kQBytes % 1024 == 0 && kScratchBytes % 1024 == 0,
+                "tiles must keep 1024-byte alignment");
 };
 
 // Barriers, ring headers and the per-warp softmax statistics of the epilogue.
@@ -145,9 +157,13 @@ __device__ __forceinline__ bool consumer_join(uint64_t* bar, uint32_t parity, in
   return warp_wait(bar, parity, status, kStatusWaitFull);
 }
 
-template <typename T, int D, int NT>
+template <typename T, int D, int NT, bool F8 = false>
 struct Kernel {
-  using C = Cfg<D, NT>;
+  using C = Cfg<D, NT, F8>;
+  // With fp8 K/V the MMAs run in f16 (every e4m3 value is exact in f16; a bf16 Q is converted
+  // on load); otherwise in the Q dtype.
+  using MT = typename std::conditional<F8, __half, T>::type;
+  using KVT = typename std::conditional<F8, uint8_t, T>::type;
   static_assert(sizeof(Misc) <= C::kMiscBytes, "misc area too small");
 
   // ------------------------------------------------------------------ scheduler (lane 0)
@@ -372,10 +388,10 @@ struct Kernel {
     const int gs = a.group_size;
     const T* qrow0 = q + static_cast<int64_t>(h.request) * a.d.q_stride[0] +
                      static_cast<int64_t>(h.group * gs) * a.d.q_stride[1];
-    if (a.fast_q) {
+    if (a.fast_q && std::is_same<MT, T>::value) {
       const uint32_t dst0 = smem_addr(qdst);
-      for (int idx = lane; idx < C::kQRows * C::kChunks; idx += 32) {
-        const int r = idx / C::kChunks, c = idx % C::kChunks;
+      for (int idx = lane; idx < C::kQRows * C::kQChunks; idx += 32) {
+        const int r = idx / C::kQChunks, c = idx % C::kQChunks;
         const bool live = r < gs;   // rows past the group read as zeros
         const T* src = qrow0 + static_cast<int64_t>(live ? r : 0) * a.d.q_stride[1] + c * 8;
         cp_async_16_fill(dst0 + tile_off<C::kQRows>(r, c), src, live ? 16u : 0u);
@@ -384,9 +400,11 @@ struct Kernel {
     } else {
       for (int idx = lane; idx < C::kQRows * D; idx += 32) {
         const int r = idx / D, d = idx % D;
-        T v = from_float<T>(0.f);
-        if (r < gs) v = qrow0[static_cast<int64_t>(r) * a.d.q_stride[1] + static_cast<int64_t>(d) * a.d.q_stride[2]];
-        *reinterpret_cast<T*>(qdst + tile_off<C::kQRows>(r, d >> 3) + (d & 7) * 2) = v;
+        MT v = from_float<MT>(0.f);
+        if (r < gs)
+          v = from_float<MT>(to_float(qrow0[static_cast<int64_t>(r) * a.d.q_stride[1] +
+                                            static_cast<int64_t>(d) * a.d.q_stride[2]]));
+        *reinterpret_cast<MT*>(qdst + tile_off<C::kQRows>(r, d >> 3) + (d & 7) * 2) = v;
       }
       mbar_arrive(bar);
     }
@@ -399,8 +417,8 @@ struct Kernel {
     // barrier traffic (the barrier counts at set-up leave them out).
     if (a.tma_kv && pw != 0) return;
     int* status = a.d.status;
-    const T* kbase = static_cast<const T*>(a.d.k);
-    const T* vbase = static_cast<const T*>(a.d.v);
+    const KVT* kbase = static_cast<const KVT*>(a.d.k);
+    const KVT* vbase = static_cast<const KVT*>(a.d.v);
     int sd = 0, s = 0, qcount = 0;
     uint32_t sph = 0, ph = 0;
     bool ok = true;
@@ -426,7 +444,7 @@ struct Kernel {
       unsigned char* stage = smem + s * C::kStageBytes;
       const uint32_t kdst = smem_addr(stage);
       const uint32_t vdst = kdst + C::kTileBytes;
-      if (a.tma_kv) {
+      if (!F8 && a.tma_kv) {
         // Tensor-map boxes: {64 dims, 1 head, R rows of one page}; only producer 0 issues.
         if (pw == 0 && lane == 0) {
           const int R = a.box_rows;
@@ -454,8 +472,8 @@ struct Kernel {
           const int jt = i * C::kTPI + lane / C::kChunks;
           if (jt < h.ntok) {
             const uint32_t off = tile_off<C::kTS>(jt, c);
-            cp_async_16(kdst + off, kbase + koff[jt] + c * 8);
-            cp_async_16(vdst + off, vbase + voff[jt] + c * 8);
+            cp_async_16(kdst + off, kbase + koff[jt] + c * C::kEPC);
+            cp_async_16(vdst + off, vbase + voff[jt] + c * C::kEPC);
           }
         }
         cp_async_arrive_noinc(&ms.full[s]);
@@ -469,9 +487,9 @@ struct Kernel {
         for (int jt = pw; jt < h.ntok; jt += C::kProducerWarps) {
           const int64_t kr = koff[jt], vr = voff[jt];
           for (int d = lane; d < D; d += 32) {
-            const uint32_t o = tile_off<C::kTS>(jt, d >> 3) + (d & 7) * 2;
-            *reinterpret_cast<T*>(stage + o) = kbase[kr + d * kd];
-            *reinterpret_cast<T*>(stage + C::kTileBytes + o) = vbase[vr + d * vd];
+            const uint32_t o = tile_off<C::kTS>(jt, d / C::kEPC) + (d % C::kEPC) * C::kKVBytes;
+            *reinterpret_cast<KVT*>(stage + o) = kbase[kr + d * kd];
+            *reinterpret_cast<KVT*>(stage + C::kTileBytes + o) = vbase[vr + d * vd];
           }
         }
         mbar_arrive(&ms.full[s]);
@@ -504,6 +522,27 @@ struct Kernel {
     __syncwarp();
   }
 
+  // fp8 K or V rows [row0, row0 + 16) of a stage tile -> this warp's f16 tile (layout
+  // [D/64][16][128 B], the one the ldmatrix reads expect).  Two lanes per row, 16-byte
+  // chunks: each fp8 chunk (16 dims) becomes two f16 chunks.
+  __device__ static void widen_rows(uint32_t src, int row0, uint32_t dst) {
+    const int lane = threadIdx.x & 31, r = lane >> 1;
+    constexpr int kPerLane = C::kChunks / 2;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+      const int c = (lane & 1) * kPerLane + i;
+      uint32_t w[4], o[8];
+      lds_v4(src + tile_off<C::kTS>(row0 + r, c), w);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        o[2 * j] = e4m3x2_to_f16x2(w[j] & 0xffffu);
+        o[2 * j + 1] = e4m3x2_to_f16x2(w[j] >> 16);
+      }
+      sts_v4(dst + tile_off<16>(r, 2 * c), o[0], o[1], o[2], o[3]);
+      sts_v4(dst + tile_off<16>(r, 2 * c + 1), o[4], o[5], o[6], o[7]);
+    }
+  }
+
   // ------------------------------------------------------------------ consumers (4 warps)
   __device__ static void consumer(const DecodeLaunch& a, unsigned char* smem, Misc& ms) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -513,7 +552,7 @@ struct Kernel {
     // both saturations (2^big = inf gives 1, 2^-big = 0 gives -1).
     const float cap = a.d.logit_cap;
     const bool capped = cap > 0.f;
-    const float sc = capped ? a.d.scale : a.d.scale * kLog2e;
+    const float sc = (capped ? a.d.scale : a.d.scale * kLog2e) * a.d.k_scale;
     const float cap_log2e = cap * kLog2e, two_log2e_over_cap = capped ? 2.f * kLog2e / cap : 0.f;
     int* status = a.d.status;
 
@@ -557,8 +596,21 @@ struct Kernel {
       const int row0 = warp * 16;
       if (row0 < h.ntok) {
         const int valid = h.ntok - row0;   // tokens of this warp's 16 that are live
-        const uint32_t kb = smem_addr(stage);
-        const uint32_t vb = kb + C::kTileBytes;
+        // K/V tiles read by ldmatrix: the stage itself, or (fp8) this warp's widened copy
+        // of its 16 rows, where they start at row 0.
+        constexpr int KR = F8 ? 16 : C::kTS;
+        const int rb = F8 ? 0 : row0;
+        uint32_t kb, vb;
+        if constexpr (F8) {
+          kb = smem_addr(smem + C::kOffScratch + warp * 2 * C::kScrTile);
+          vb = kb + C::kScrTile;
+          widen_rows(smem_addr(stage), row0, kb);
+          widen_rows(smem_addr(stage) + C::kTileBytes, row0, vb);
+          __syncwarp();
+        } else {
+          kb = smem_addr(stage);
+          vb = kb + C::kTileBytes;
+        }
         // ---- S^T = K Q^T  (two independent accumulator chains)
         float sa[NT][4], sb[NT][4];
 #pragma unroll
@@ -567,14 +619,14 @@ struct Kernel {
           for (int i = 0; i < 4; ++i) sa[nt][i] = sb[nt][i] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
-          const int row = row0 + (lane & 15);
+          const int row = rb + (lane & 15);
           const int chunk = 2 * ks + (lane >> 4);
           uint32_t a0, a1, a2, a3;
-          ldsm_x4(kb + tile_off<C::kTS>(row, chunk), a0, a1, a2, a3);
+          ldsm_x4(kb + tile_off<KR>(row, chunk), a0, a1, a2, a3);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            if (ks & 1) Mma<T>::run(sb[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
-            else Mma<T>::run(sa[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
+            if (ks & 1) Mma<MT>::run(sb[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
+            else Mma<MT>::run(sa[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
           }
         }
         // ---- online softmax (log2 domain); masked tokens score -inf whatever K held
@@ -608,8 +660,8 @@ struct Kernel {
               o[mt][nt][jj + 2] *= alpha;
             }
           }
-          pb[nt][0] = movmatrix_t(Mma<T>::pack(sv[0], sv[1]));
-          pb[nt][1] = movmatrix_t(Mma<T>::pack(sv[2], sv[3]));
+          pb[nt][0] = movmatrix_t(Mma<MT>::pack(sv[0], sv[1]));
+          pb[nt][1] = movmatrix_t(Mma<MT>::pack(sv[2], sv[3]));
         }
         // ---- O^T += V^T P^T; on a partial tile the V rows past the last token are
         //      zeroed in the fragments (their P is already zero, stale data may not be).
@@ -618,10 +670,10 @@ struct Kernel {
         const uint32_t mhi = (2 * t4 + 8 < valid ? 0x0000ffffu : 0u) | (2 * t4 + 9 < valid ? 0xffff0000u : 0u);
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
-          const int row = row0 + (lane & 7) + ((lane >> 4) << 3);
+          const int row = rb + (lane & 7) + ((lane >> 4) << 3);
           const int chunk = 2 * mt + ((lane >> 3) & 1);
           uint32_t a0, a1, a2, a3;
-          ldsm_x4_t(vb + tile_off<C::kTS>(row, chunk), a0, a1, a2, a3);
+          ldsm_x4_t(vb + tile_off<KR>(row, chunk), a0, a1, a2, a3);
           if (partial) {
             a0 &= mlo;
             a1 &= mlo;
@@ -629,7 +681,7 @@ struct Kernel {
             a3 &= mhi;
           }
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) Mma<T>::run(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+          for (int nt = 0; nt < NT; ++nt) Mma<MT>::run(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
         }
       }
       __syncwarp();
@@ -710,7 +762,8 @@ struct Kernel {
         v.z += r.z * sw[w];
         v.w += r.w * sw[w];
       }
-      const float4 res = make_float4(v.x / gl, v.y / gl, v.z / gl, v.w / gl);
+      const float vs = a.d.v_scale;
+      const float4 res = make_float4(v.x / gl * vs, v.y / gl * vs, v.z / gl * vs, v.w / gl * vs);
       const int64_t slot = slot0 + static_cast<int64_t>(head) * smax;
       *reinterpret_cast<float4*>(a.d.partial + slot * D + d) = res;   // 16-byte aligned (checked at entry)
       if (d == 0) a.d.lse[slot] = (gm + lg2(gl)) * kLn2;
@@ -782,20 +835,25 @@ struct Kernel {
   }
 };
 
-template <typename T, int D, int NT>
-__global__ void __launch_bounds__(Cfg<D, NT>::kThreads, 1) decode_kernel(const __grid_constant__ DecodeLaunch a) {
-  Kernel<T, D, NT>::run(a);
+template <typename T, int D, int NT, bool F8>
+__global__ void __launch_bounds__(Cfg<D, NT, F8>::kThreads, 1) decode_kernel(const __grid_constant__ DecodeLaunch a) {
+  Kernel<T, D, NT, F8>::run(a);
 }
 
-template <typename T, int D, int NT>
+template <typename T, int D, int NT, bool F8>
 cudaError_t launch_typed(const DecodeLaunch& a, cudaStream_t stream) {
-  using C = Cfg<D, NT>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes);
+  using C = Cfg<D, NT, F8>;
+  constexpr int kMaxDevices = 64;
+  static bool configured[kMaxDevices] = {};   // the smem attribute is per device
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!configured[device]) {
+    e = cudaFuncSetAttribute(decode_kernel<T, D, NT, F8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::kSmemBytes);
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured[device] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.workers);
@@ -807,16 +865,20 @@ cudaError_t launch_typed(const DecodeLaunch& a, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NT>, a);
+  return cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NT, F8>, a);
 }
 
 template <typename T>
 cudaError_t launch_dtype(const DecodeLaunch& a, cudaStream_t stream) {
   const bool wide = a.group_size > 8;
+  if (a.kv_fp8) {   // e4m3 K/V: head_dim 128 only (checked by the caller)
+    if (a.d.head_dim != 128) return cudaErrorInvalidValue;
+    return wide ? launch_typed<T, 128, 2, true>(a, stream) : launch_typed<T, 128, 1, true>(a, stream);
+  }
   switch (a.d.head_dim) {
-    case 64: return wide ? launch_typed<T, 64, 2>(a, stream) : launch_typed<T, 64, 1>(a, stream);
-    case 128: return wide ? launch_typed<T, 128, 2>(a, stream) : launch_typed<T, 128, 1>(a, stream);
-    case 256: return wide ? launch_typed<T, 256, 2>(a, stream) : launch_typed<T, 256, 1>(a, stream);
+    case 64: return wide ? launch_typed<T, 64, 2, false>(a, stream) : launch_typed<T, 64, 1, false>(a, stream);
+    case 128: return wide ? launch_typed<T, 128, 2, false>(a, stream) : launch_typed<T, 128, 1, false>(a, stream);
+    case 256: return wide ? launch_typed<T, 256, 2, false>(a, stream) : launch_typed<T, 256, 1, false>(a, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -38,6 +38,7 @@ struct alignas(64) DecodeLaunch {
   int32_t csr;
   int32_t fast_kv;   // K/V rows are 16-byte aligned, unit stride along D
   int32_t fast_q;    // Q rows are 16-byte aligned, unit stride along D
+  int32_t kv_fp8;    // K/V are e4m3 (Q and the output are fp16/bf16)
   int32_t tma_kv;    // paged KV loaded by tensor-map TMA boxes of box_rows tokens
   int32_t box_rows;
 };

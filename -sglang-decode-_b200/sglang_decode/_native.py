@@ -41,16 +41,17 @@ class DecodeArgs(ctypes.Structure):
         ("kv_extent", ctypes.c_int64),
         ("dtype", ctypes.c_int32), ("query_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
         ("head_dim", ctypes.c_int32), ("page_size", ctypes.c_int32), ("scale", ctypes.c_float), ("logit_cap", ctypes.c_float),
+        ("kv_dtype", ctypes.c_int32), ("k_scale", ctypes.c_float), ("v_scale", ctypes.c_float),
         ("counter", ctypes.c_void_p), ("partial", ctypes.c_void_p), ("lse", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
     ]
 
 
-DTYPE_F16, DTYPE_BF16 = 0, 1
+DTYPE_F16, DTYPE_BF16, DTYPE_E4M3 = 0, 1, 2
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error"}
 EXPORTS = ("sgld_abi_version", "sgld_last_error", "sgld_layer_workspace_bytes", "sgld_plan_build",
            "sgld_decode_persistent", "sgld_merge_splits")
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 _lock = threading.Lock()
 _lib = None

@@ -20,6 +20,7 @@ from ..planning.builder import build_plan
 from .workspace import LayerBuffers, PlanBuffers
 
 _DTYPES = {torch.float16: _native.DTYPE_F16, torch.bfloat16: _native.DTYPE_BF16}
+_FP8 = getattr(torch, "float8_e4m3fn", None)
 
 
 @dataclass(frozen=True)
@@ -48,17 +49,23 @@ class DecodeEngine:
         """Call once per compatible group per step, including on every graph replay."""
         build_plan(self.plan, self.force_mode)
 
-    def execute(self, q, k, v, pages, layer=0, *, indptr=None, scale=None, logit_cap=0.0):
+    def execute(self, q, k, v, pages, layer=0, *, indptr=None, scale=None, logit_cap=0.0,
+                k_scale=1.0, v_scale=1.0):
         """KV layout: [pages,page_size,kv_heads,D], or CSR [tokens,kv_heads,D].
 
         Metadata and Q/KV must be ready on the current CUDA stream. Fixed buffers
         are reused; consumers must finish before reusing this execution instance.
         ``logit_cap`` > 0 soft-caps the scaled scores, s -> cap * tanh(s / cap), as SGLang
         does for models such as Gemma-2 (an addition: the reference has no capped path).
+        K/V may be fp8 (``torch.float8_e4m3fn``, head_dim 128) with a fp16/bf16 Q: scores
+        then use ``k_scale * k`` and the output ``v_scale * v`` (also an addition).
         """
         c, p, out = self.config, self.plan, self.layers[layer]
-        if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
-            raise ValueError("BF16/FP16 Q/K/V of identical dtype are required")
+        kv_fp8 = k.dtype == _FP8
+        if q.dtype not in _DTYPES or v.dtype != k.dtype or (k.dtype != q.dtype and not kv_fp8):
+            raise ValueError("BF16/FP16 Q/K/V of identical dtype are required (or fp8 e4m3 K/V)")
+        if kv_fp8 and c.head_dim != 128:
+            raise ValueError("fp8 K/V are supported for head_dim 128")
         if tuple(q.shape) != (c.batch_capacity, c.query_heads, c.head_dim):
             raise ValueError("Q must use the capture capacity; pad inactive rows")
         if out.output.dtype != q.dtype:
@@ -99,6 +106,12 @@ class DecodeEngine:
         a.kv_extent = k.shape[0] if k.shape[0] == v.shape[0] else 0
         a.q_stride[:] = q.stride()
         a.dtype = _DTYPES[q.dtype]
+        a.kv_dtype = _native.DTYPE_E4M3 if kv_fp8 else a.dtype
+        for name, value in (("k_scale", k_scale), ("v_scale", v_scale)):
+            value = float(value)
+            if not value > 0.0 or value == float("inf"):
+                raise ValueError(f"{name} must be a finite value > 0")
+            setattr(a, name, value)
         a.query_heads, a.kv_heads, a.head_dim = c.query_heads, c.kv_heads, c.head_dim
         a.scale = c.head_dim ** -0.5 if scale is None else float(scale)
         cap = float(logit_cap or 0.0)

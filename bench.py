@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--requests", type=int, default=None,
                     help="profile a prefix sub-workload (first N requests); not a bench line")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--kv-dtype", choices=["q", "fp8"], default="q",
+                    help="K/V pool dtype: the Q dtype (the reference's), or e4m3 with unit scales")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -138,13 +140,14 @@ def traffic_ratio(workload):
     return None
 
 
-def algorithmic_bytes(b, kv_heads_local, q_heads_local):
-    """Σ L·Hkv·D·2(K,V)·elem + Q + O + index bytes (4·ΣL CSR, 4·Σceil(L/ps) paged)."""
+def algorithmic_bytes(b, kv_heads_local, q_heads_local, kv_elem=None):
+    """Σ L·Hkv·D·2(K,V)·kv_elem + Q + O + index bytes (4·ΣL CSR, 4·Σceil(L/ps) paged)."""
     import torch
     elem = torch.finfo(b.dtype).bits // 8
+    kv_elem = elem if kv_elem is None else kv_elem
     c = b.config
     total = sum(b.lengths)
-    kv = total * kv_heads_local * c.head_dim * 2 * elem
+    kv = total * kv_heads_local * c.head_dim * 2 * kv_elem
     qo = 2 * len(b.lengths) * q_heads_local * c.head_dim * elem
     idx = 4 * total if b.csr else 4 * sum(math.ceil(n / c.page_size) for n in b.lengths)
     return kv + qo + idx
@@ -270,6 +273,11 @@ def run_ours(args):
                           rules=load_policy(args.policy))
     update_plan(engine, b.lengths, b.splits)
     q, k, v, pages, indptr = data["q"], data["k"], data["v"], data["pages"], data["indptr"]
+    fp8 = args.kv_dtype == "fp8"
+    if fp8:                                   # e4m3 pool of the same values, unit scales
+        k, v = k.to(torch.float8_e4m3fn), v.to(torch.float8_e4m3fn)
+        del data
+        torch.cuda.empty_cache()
 
     def step():
         engine.prepare()
@@ -357,11 +365,11 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     step_ms, dec_ms, e2e_ms = stats.tolist()
-    bytes_launch = algorithmic_bytes(b, hkv, hq)
+    bytes_launch = algorithmic_bytes(b, hkv, hq, kv_elem=1 if fp8 else None)
     achieved = bytes_launch / (dec_ms * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
     clock = clocks.summary()
-    ratio = traffic_ratio(args.workload) if args.requests is None and world == 1 else None
+    ratio = traffic_ratio(args.workload) if args.requests is None and world == 1 and not fp8 else None
     traffic = int(ratio * bytes_launch) if ratio else None
 
     if rank == 0:
@@ -378,7 +386,7 @@ def run_ours(args):
             "data": "synthetic",
             "config": {"workload": f"{b.name}: B={len(b.lengths)} Hq={c.query_heads} Hkv={c.kv_heads} "
                                    f"D={c.head_dim} {'CSR' if b.csr else f'paged ps={c.page_size}'} "
-                                   f"sum(L)={sum(b.lengths)}",
+                                   f"sum(L)={sum(b.lengths)}" + (" KV e4m3" if fp8 else ""),
                        "mode": "AUTO" if args.mode < 0 else args.mode,
                        "policy": Path(args.policy).name if args.policy else None,
                        "heads_per_gpu": {"kv": hkv, "q": hq}, "workers": sms,

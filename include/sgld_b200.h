@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define SGLD_ABI_VERSION 4
+#define SGLD_ABI_VERSION 5
 
 typedef enum sgld_status {
   SGLD_OK = 0,
@@ -38,7 +38,7 @@ typedef enum sgld_status {
   SGLD_ERR_CUDA = 3              /* a launch failed; see sgld_last_error()           */
 } sgld_status;
 
-enum { SGLD_DTYPE_F16 = 0, SGLD_DTYPE_BF16 = 1 };
+enum { SGLD_DTYPE_F16 = 0, SGLD_DTYPE_BF16 = 1, SGLD_DTYPE_E4M3 = 2 /* K/V only: fp8 e4m3 */ };
 
 /* Execution modes -- reference src/sglang_decode/config.py:6-11. */
 enum { SGLD_MODE_R0 = 0, SGLD_MODE_R1 = 1, SGLD_MODE_STATIC = 2, SGLD_MODE_D1 = 3, SGLD_MODE_D4 = 4 };
@@ -117,6 +117,10 @@ typedef struct sgld_decode_args {
                            before the softmax (SGLang's soft cap, upstream
                            decode_attention.py:127-128); 0 disables it; not in the
                            reference's own kernel (its adapter falls back)              */
+  int32_t kv_dtype;     /* dtype of k and v: == dtype, or SGLD_DTYPE_E4M3 (fp8 K/V with a
+                           fp16/bf16 q; head_dim 128).  The reference has no fp8 path      */
+  float k_scale;        /* scores use k_scale * k (0 reads as 1): dequantises fp8 keys      */
+  float v_scale;        /* outputs use v_scale * v (0 reads as 1)                           */
   /* Layer scratch -- reference runtime/workspace.py:26-40 (LayerBuffers) */
   int32_t* counter;     /* [2]  claim counter + exit ticket; zero before, left zero after    */
   float* partial;       /* [B, Hq, Smax, D] fp32 normalised split outputs, 16-byte aligned   */

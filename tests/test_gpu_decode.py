@@ -25,14 +25,16 @@ MIXED = [0, 1, 17, 33, 257, 513]
 B = [256] * 24 + [1536] * 4 + [16384] * 4
 
 
-def run(engine, inputs, lengths, splits=None, indptr=None, layer=0, scale=None, logit_cap=0.0):
+def run(engine, inputs, lengths, splits=None, indptr=None, layer=0, scale=None, logit_cap=0.0, k_scale=1.0,
+        v_scale=1.0):
     update_plan(engine, lengths, splits)
     lb = engine.layers[layer]
     lb.partial.fill_(float("nan"))
     lb.lse.fill_(float("nan"))
     engine.prepare()
     q, k, v, pages = inputs
-    out = engine.execute(q, k, v, pages, layer=layer, indptr=indptr, scale=scale, logit_cap=logit_cap)
+    out = engine.execute(q, k, v, pages, layer=layer, indptr=indptr, scale=scale, logit_cap=logit_cap,
+                         k_scale=k_scale, v_scale=v_scale)
     torch.cuda.synchronize()
     assert lb.status.item() == 0, "bounded in-kernel wait expired"
     assert engine.counters.eq(0).all(), "claim counter / exit ticket not left at zero"
@@ -143,6 +145,65 @@ def test_logit_soft_cap_matches_oracle_in_every_mode(cap, layout, cuda_device):
         assert_within_tolerance(out, expected, len(lengths))
         outs.append(out.clone())
     assert all(torch.equal(outs[0], o) for o in outs[1:]), "every dispatch mode gives identical outputs"
+
+
+FP8 = getattr(torch, "float8_e4m3fn", None)
+
+
+@pytest.mark.skipif(FP8 is None, reason="torch without float8_e4m3fn")
+@pytest.mark.parametrize("qdtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("layout", ["csr_g8", "csr_g7", "csr_g16", "paged16_g4", "paged64_g8", "csr_strided_g4"])
+@pytest.mark.parametrize("scales", [(1.0, 1.0), (0.5, 2.0)], ids=["unscaled", "scaled"])
+def test_fp8_kv_matches_oracle_in_every_mode(qdtype, layout, scales, cuda_device):
+    """e4m3 K/V with a fp16/bf16 Q: the oracle sees the same fp8 values (dequantised, times
+    k_scale / v_scale); every dispatch mode gives identical outputs."""
+    lengths = [1, 65, 300, 0, 1000, 129, 700]
+    group, hkv = {"csr_g8": (8, 2), "csr_g7": (7, 2), "csr_g16": (16, 1), "paged16_g4": (4, 4),
+                  "paged64_g8": (8, 2), "csr_strided_g4": (4, 2)}[layout]
+    ps = {"paged16_g4": 16, "paged64_g8": 64}.get(layout, 1)
+    c = DecodeConfig(batch_capacity=8, max_splits=8, max_context=1024, query_heads=hkv * group,
+                     kv_heads=hkv, head_dim=128, page_size=ps, workers=37)
+    ks, vs = scales
+    if ps == 1:
+        q, k, v, idx, indptr = (t.cuda() for t in make_csr_inputs(c, lengths, device="cpu", dtype=qdtype,
+                                                                   pool=4000))
+        k8, v8 = k.to(FP8), v.to(FP8)
+        if layout == "csr_strided_g4":                 # rows 160 bytes apart: the element-copy path
+            wide_k = torch.zeros(k.shape[0], hkv, 160, device="cuda", dtype=FP8)
+            wide_v = torch.zeros_like(wide_k)
+            wide_k[..., :128], wide_v[..., :128] = k8, v8
+            k8, v8 = wide_k[..., :128], wide_v[..., :128]
+        pages = idx
+        expected = oracle_csr(q, k8.float() * ks, v8.float() * vs, indptr, idx, lengths)
+    else:
+        indptr = None
+        q, k, v, pages = (t.cuda() for t in make_inputs(c, lengths, device="cpu", dtype=qdtype))
+        k8, v8 = k.to(FP8), v.to(FP8)
+        expected = oracle_paged(q, k8.float() * ks, v8.float() * vs, pages, lengths, ps)
+    outs = []
+    for mode in (Mode.R0, Mode.R1, Mode.STATIC, Mode.D1, Mode.D4):
+        out = run(DecodeEngine(c, dtype=qdtype, force_mode=mode), (q, k8, v8, pages), lengths, indptr=indptr,
+                  k_scale=ks, v_scale=vs)
+        assert_within_tolerance(out, expected, len(lengths))
+        outs.append(out.clone())
+    assert all(torch.equal(outs[0], o) for o in outs[1:]), "every dispatch mode gives identical outputs"
+
+
+@pytest.mark.skipif(FP8 is None, reason="torch without float8_e4m3fn")
+def test_fp8_kv_rejects_other_head_dims_and_mixed_kv(cuda_device):
+    lengths = [10, 20]
+    c = DecodeConfig(batch_capacity=2, max_splits=2, max_context=64, query_heads=8, kv_heads=2,
+                     head_dim=64, page_size=1, workers=4)
+    q, k, v, idx, indptr = (t.cuda() for t in make_csr_inputs(c, lengths, device="cpu", pool=64))
+    engine = DecodeEngine(c)
+    update_plan(engine, lengths)
+    engine.prepare()
+    with pytest.raises(ValueError):                    # fp8 K/V: head_dim 128 only
+        engine.execute(q, k.to(FP8), v.to(FP8), idx, indptr=indptr)
+    with pytest.raises(ValueError):                    # K and V must share a dtype
+        engine.execute(q, k.to(FP8), v, idx, indptr=indptr)
+    with pytest.raises(ValueError):
+        engine.execute(q, k, v, idx, indptr=indptr, k_scale=0.0)
 
 
 def test_logit_cap_must_be_finite_and_non_negative(cuda_device):

@@ -68,6 +68,9 @@ def test_host_checks_reject_bad_arguments_without_touching_a_gpu(lib):
     args.q = args.k = args.v = args.out = args.pages = 16
     args.counter = args.partial = args.lse = args.status = 16
     args.dtype, args.query_heads, args.kv_heads, args.head_dim, args.page_size = 1, 32, 8, 96, 16
+    assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 1
+    assert b"kv_dtype" in lib.sgld_last_error()                # K/V dtype must match q or be e4m3
+    args.kv_dtype = args.dtype
     args.partial = 20                                          # the epilogue and merge store float4 rows
     assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 1
     assert b"16-byte aligned" in lib.sgld_last_error()
@@ -77,6 +80,15 @@ def test_host_checks_reject_bad_arguments_without_touching_a_gpu(lib):
         assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 1
         assert b"logit_cap" in lib.sgld_last_error()
     args.logit_cap = 0.0
+    for name in ("k_scale", "v_scale"):                         # scales: finite and >= 0
+        setattr(args, name, -2.0)
+        assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 1
+        setattr(args, name, 0.0)
+    assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 2
+    args.kv_dtype, args.head_dim = _native.DTYPE_E4M3, 64        # fp8 K/V: head_dim 128 only
+    assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 2
+    assert b"fp8" in lib.sgld_last_error()
+    args.kv_dtype, args.head_dim = args.dtype, 96
     assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 2
     assert b"head dimensions" in lib.sgld_last_error()
     args.head_dim, args.query_heads = 128, 8 * 17
@@ -96,7 +108,8 @@ int main(void) {
   printf("sgld_decode_args %zu\n", sizeof(sgld_decode_args));
   F(sgld_plan_geometry, workers) F(sgld_plan_buffers, static_next)
   F(sgld_decode_args, q_stride) F(sgld_decode_args, kv_extent) F(sgld_decode_args, dtype)
-  F(sgld_decode_args, scale) F(sgld_decode_args, logit_cap) F(sgld_decode_args, counter) F(sgld_decode_args, partial)
+  F(sgld_decode_args, scale) F(sgld_decode_args, logit_cap) F(sgld_decode_args, kv_dtype)
+  F(sgld_decode_args, k_scale) F(sgld_decode_args, v_scale) F(sgld_decode_args, counter) F(sgld_decode_args, partial)
   F(sgld_decode_args, lse) F(sgld_decode_args, status)
   return 0;
 }
@@ -117,6 +130,7 @@ def test_ctypes_structs_match_the_c_header(tmp_path):
         "sgld_plan_geometry.workers": _native.PlanGeometry.workers.offset,
         "sgld_plan_buffers.static_next": _native.PlanBuffersC.static_next.offset,
     }
-    for field in ("q_stride", "kv_extent", "dtype", "scale", "logit_cap", "counter", "partial", "lse", "status"):
+    for field in ("q_stride", "kv_extent", "dtype", "scale", "logit_cap", "kv_dtype", "k_scale", "v_scale",
+                  "counter", "partial", "lse", "status"):
         want[f"sgld_decode_args.{field}"] = getattr(_native.DecodeArgs, field).offset
     assert {k: int(v) for k, v in got.items()} == want
