@@ -72,9 +72,7 @@ struct Cfg {
   // as many producer warps as the register file allows next to the consumers (16 warps
   // at 128 registers for D <= 128 and a group of at most 8).  With tensor-map copies
   // producer 0 works alone.
-  // fp8 stages carry half the bytes; its 16-row-group kernel keeps 4 producers so the
-  // widening consumers fit in registers.
-  static constexpr int kProducerWarps = kBig ? 2 : (NT == 2 ? (F8 ? 4 : 5) : (D >= 256 ? 6 : 10));
+  static constexpr int kProducerWarps = kBig ? 2 : (NT == 2 ? 5 : (D >= 256 ? 6 : 10));
   static constexpr int kProducerWarp0 = kConsumerWarps;
   static constexpr int kIndexerWarp = kProducerWarp0 + kProducerWarps;
   static constexpr int kSchedulerWarp = kIndexerWarp + 1;
@@ -100,25 +98,24 @@ struct Cfg {
   static constexpr int kSDEntry = kTS * 24;              // koff, voff (int64), page, row (int32)
   static constexpr int kSDBytes = kSD * kSDEntry;
   static constexpr int kMiscBytes = 4096;
-  // fp8 K/V: each consumer warp widens its 16 rows of K and V to f16 here before the MMAs.
-  static constexpr int kScrTile = F8 ? 16 * D * 2 : 0;
-  static constexpr int kScratchBytes = 2 * kConsumerWarps * kScrTile;
-  static constexpr int kFixed1 = 2 * kQBytes + kSDBytes + kMiscBytes + kScratchBytes;
+  static constexpr int kFixed1 = 2 * kQBytes + kSDBytes + kMiscBytes;
   static constexpr int kRedBufs = (kFixed1 + 2 * kRedOne + 3 * kStageBytes <= kSmemBudget) ? 2 : 1;
   static constexpr int kFixed = kFixed1 + kRedBufs * kRedOne;
   static constexpr int kStagesRaw = (kSmemBudget - kFixed) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  // Consumers hold two stages at a time (paired stages) when the ring is deep enough; the
+  // 16-row-group kernels have no registers to spare for the second sub-tile.
+  static constexpr bool kPair = kStages >= 4 && NT == 1;
   static_assert(kStages >= 2, "shared memory budget too small");
   // Offsets from the 1024-byte aligned base (tiles first: they need the alignment).
-  static constexpr int kOffScratch = kStages * kStageBytes;
-  static constexpr int kOffQ = kOffScratch + kScratchBytes;
+  static constexpr int kOffQ = kStages * kStageBytes;
   static constexpr int kOffRed = kOffQ + 2 * kQBytes;
   static constexpr int kOffSD = kOffRed + kRedBufs * kRedOne;
   static constexpr int kOffMisc = kOffSD + kSDBytes;
   static constexpr int kSmemUsed = kOffMisc + kMiscBytes;
   static constexpr int kSmemBytes = kSmemUsed + 1024;    // launch size including alignment slack
   static_assert(kSmemUsed <= kSmemBudget, "shared memory budget exceeded");
-  static_assert(kTileBytes % 1024 == 0 && kQBytes % 1024 == 0 && kScratchBytes % 1024 == 0,
+  static_assert(kTileBytes % 1024 == 0 && kQBytes % 1024 == 0,
                 "tiles must keep 1024-byte alignment");
 };
 
@@ -522,27 +519,6 @@ struct Kernel {
     __syncwarp();
   }
 
-  // fp8 K or V rows [row0, row0 + 16) of a stage tile -> this warp's f16 tile (layout
-  // [D/64][16][128 B], the one the ldmatrix reads expect).  Two lanes per row, 16-byte
-  // chunks: each fp8 chunk (16 dims) becomes two f16 chunks.
-  __device__ static void widen_rows(uint32_t src, int row0, uint32_t dst) {
-    const int lane = threadIdx.x & 31, r = lane >> 1;
-    constexpr int kPerLane = C::kChunks / 2;
-#pragma unroll
-    for (int i = 0; i < kPerLane; ++i) {
-      const int c = (lane & 1) * kPerLane + i;
-      uint32_t w[4], o[8];
-      lds_v4(src + tile_off<C::kTS>(row0 + r, c), w);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        o[2 * j] = e4m3x2_to_f16x2(w[j] & 0xffffu);
-        o[2 * j + 1] = e4m3x2_to_f16x2(w[j] >> 16);
-      }
-      sts_v4(dst + tile_off<16>(r, 2 * c), o[0], o[1], o[2], o[3]);
-      sts_v4(dst + tile_off<16>(r, 2 * c + 1), o[4], o[5], o[6], o[7]);
-    }
-  }
-
   // ------------------------------------------------------------------ consumers (4 warps)
   __device__ static void consumer(const DecodeLaunch& a, unsigned char* smem, Misc& ms) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -576,10 +552,22 @@ struct Kernel {
         for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
           for (int ks = 0; ks < KS; ks += 2) {
-            const int row = nt * 8 + (lane & 7);
-            const int chunk = 2 * ks + (lane >> 3);
-            ldsm_x4(qbase + tile_off<C::kQRows>(row, chunk), qf[nt][ks][0], qf[nt][ks][1],
-                    qf[nt][ks + 1][0], qf[nt][ks + 1][1]);
+            if constexpr (F8) {
+              // Contraction order of the fp8 K fragments (below): k-step ks, B rows 2*t4 + {0,1}
+              // and 8 + 2*t4 + {0,1} are dims 32*t4 + 4*ks + {0,1} and {2,3}.  Lane (g8, t4)
+              // reads query row g8's dims [32*t4 + 4*ks, +8), i.e. chunk 4*t4 + ks/2.
+              uint32_t w[4];
+              lds_v4(qbase + tile_off<C::kQRows>(nt * 8 + g8, 4 * t4 + ks / 2), w);
+              qf[nt][ks][0] = w[0];
+              qf[nt][ks][1] = w[1];
+              qf[nt][ks + 1][0] = w[2];
+              qf[nt][ks + 1][1] = w[3];
+            } else {
+              const int row = nt * 8 + (lane & 7);
+              const int chunk = 2 * ks + (lane >> 3);
+              ldsm_x4(qbase + tile_off<C::kQRows>(row, chunk), qf[nt][ks][0], qf[nt][ks][1],
+                      qf[nt][ks + 1][0], qf[nt][ks + 1][1]);
+            }
           }
         }
         __syncwarp();
@@ -593,66 +581,62 @@ struct Kernel {
         }
       }
 
+      // Paired stages: a stage that is not its task's last is followed in the ring by the
+      // task's next stage; the warp takes its 16 rows of both, so one softmax update, one O
+      // rescale and one set of shuffles cover 32 tokens and the two sub-tiles' MMAs overlap.
+      // Pairs restart at every task, so the arithmetic does not depend on the dispatch mode.
       const int row0 = warp * 16;
-      if (row0 < h.ntok) {
-        const int valid = h.ntok - row0;   // tokens of this warp's 16 that are live
-        // K/V tiles read by ldmatrix: the stage itself, or (fp8) this warp's widened copy
-        // of its 16 rows, where they start at row 0.
-        constexpr int KR = F8 ? 16 : C::kTS;
-        const int rb = F8 ? 0 : row0;
-        uint32_t kb, vb;
-        if constexpr (F8) {
-          kb = smem_addr(smem + C::kOffScratch + warp * 2 * C::kScrTile);
-          vb = kb + C::kScrTile;
-          widen_rows(smem_addr(stage), row0, kb);
-          widen_rows(smem_addr(stage) + C::kTileBytes, row0, vb);
-          __syncwarp();
-        } else {
-          kb = smem_addr(stage);
-          vb = kb + C::kTileBytes;
-        }
-        // ---- S^T = K Q^T  (two independent accumulator chains)
-        float sa[NT][4], sb[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) sa[nt][i] = sb[nt][i] = 0.f;
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-          const int row = rb + (lane & 15);
-          const int chunk = 2 * ks + (lane >> 4);
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(kb + tile_off<KR>(row, chunk), a0, a1, a2, a3);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            if (ks & 1) Mma<MT>::run(sb[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
-            else Mma<MT>::run(sa[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
-          }
-        }
-        // ---- online softmax (log2 domain); masked tokens score -inf whatever K held
-        uint32_t pb[NT][2];
+      const bool pair = C::kPair && !(h.flags & kFlagLast);
+      int s2 = s + 1;
+      uint32_t ph2 = ph;
+      if (s2 == C::kStages) {
+        s2 = 0;
+        ph2 ^= 1u;
+      }
+      int flags2 = 0, ntok2 = 0;
+      if (pair) {
+        if (!warp_wait(&ms.full[s2], ph2, status, kStatusWaitFull)) return;
+        flags2 = ms.hdr[s2].flags;
+        ntok2 = ms.hdr[s2].ntok;
+      }
+      const int valid_a = h.ntok - row0;            // live tokens of this warp's rows in each
+      const int valid_b = pair ? ntok2 - row0 : 0;  // stage (a non-last stage is full)
+      if (valid_a > 0) {
+        const uint32_t ka = smem_addr(stage), kb2 = smem_addr(smem + s2 * C::kStageBytes);
+        const bool has_b = valid_b > 0;
+        float sv[2][NT][4];
+        qk_tile(ka, row0, qf, sv[0]);
+        if (has_b) qk_tile(kb2, row0, qf, sv[1]);
+        // ---- online softmax (log2 domain) over both sub-tiles; masked tokens score -inf
+        uint32_t pb[2][NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          float sv[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int tok = g8 + (i >= 2 ? 8 : 0);
-            float x = (sa[nt][i] + sb[nt][i]) * sc;
-            if (capped) x = cap_log2e * (1.f - 2.f / (ex2(x * two_log2e_over_cap) + 1.f));
-            sv[i] = tok < valid ? x : -INFINITY;
-          }
+          for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int tok = g8 + (i >= 2 ? 8 : 0);
+              float x = sv[u][nt][i] * sc;
+              if (capped) x = cap_log2e * (1.f - 2.f / (ex2(x * two_log2e_over_cap) + 1.f));
+              sv[u][nt][i] = tok < (u == 0 ? valid_a : valid_b) ? x : -INFINITY;
+            }
 #pragma unroll
           for (int jj = 0; jj < 2; ++jj) {
-            float mx = fmaxf(sv[jj], sv[jj + 2]);
+            float mx = fmaxf(fmaxf(sv[0][nt][jj], sv[0][nt][jj + 2]), fmaxf(sv[1][nt][jj], sv[1][nt][jj + 2]));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
             const float mnew = fmaxf(m[nt][jj], mx);
             const float alpha = ex2(m[nt][jj] - mnew);   // ex2(-inf) == 0 on the first tile
-            const float p0 = ex2(sv[jj] - mnew), p1 = ex2(sv[jj + 2] - mnew);
-            sv[jj] = p0;
-            sv[jj + 2] = p1;
-            lsum[nt][jj] = lsum[nt][jj] * alpha + p0 + p1;
+            float psum = 0.f;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float p0 = ex2(sv[u][nt][jj] - mnew), p1 = ex2(sv[u][nt][jj + 2] - mnew);
+              sv[u][nt][jj] = p0;
+              sv[u][nt][jj + 2] = p1;
+              psum += p0 + p1;
+            }
+            lsum[nt][jj] = lsum[nt][jj] * alpha + psum;
             m[nt][jj] = mnew;
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) {
@@ -660,41 +644,140 @@ struct Kernel {
               o[mt][nt][jj + 2] *= alpha;
             }
           }
-          pb[nt][0] = movmatrix_t(Mma<MT>::pack(sv[0], sv[1]));
-          pb[nt][1] = movmatrix_t(Mma<MT>::pack(sv[2], sv[3]));
-        }
-        // ---- O^T += V^T P^T; on a partial tile the V rows past the last token are
-        //      zeroed in the fragments (their P is already zero, stale data may not be).
-        const bool partial = valid < 16;
-        const uint32_t mlo = (2 * t4 < valid ? 0x0000ffffu : 0u) | (2 * t4 + 1 < valid ? 0xffff0000u : 0u);
-        const uint32_t mhi = (2 * t4 + 8 < valid ? 0x0000ffffu : 0u) | (2 * t4 + 9 < valid ? 0xffff0000u : 0u);
 #pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-          const int row = rb + (lane & 7) + ((lane >> 4) << 3);
-          const int chunk = 2 * mt + ((lane >> 3) & 1);
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4_t(vb + tile_off<KR>(row, chunk), a0, a1, a2, a3);
-          if (partial) {
-            a0 &= mlo;
-            a1 &= mlo;
-            a2 &= mhi;
-            a3 &= mhi;
+          for (int u = 0; u < 2; ++u) {
+            pb[u][nt][0] = movmatrix_t(Mma<MT>::pack(sv[u][nt][0], sv[u][nt][1]));
+            pb[u][nt][1] = movmatrix_t(Mma<MT>::pack(sv[u][nt][2], sv[u][nt][3]));
           }
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) Mma<MT>::run(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
         }
+        // ---- O^T += V^T P^T per sub-tile
+        pv_tile(smem_addr(stage) + C::kTileBytes, row0, valid_a, pb[0], o);
+        if (has_b) pv_tile(smem_addr(smem + s2 * C::kStageBytes) + C::kTileBytes, row0, valid_b, pb[1], o);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ms.empty[s]);
+      if (lane == 0) {
+        mbar_arrive(&ms.empty[s]);
+        if (pair) mbar_arrive(&ms.empty[s2]);
+      }
 
-      if (h.flags & kFlagLast) {
+      if ((pair ? flags2 : h.flags) & kFlagLast) {
         if (!epilogue(a, smem, ms, h, task_idx, o, m, lsum)) return;
         ++task_idx;
+      }
+      if (pair) {
+        s = s2;
+        ph = ph2;
       }
       if (++s == C::kStages) {
         s = 0;
         ph ^= 1u;
       }
+    }
+  }
+
+  // S^T = K Q^T for rows [row0, row0 + 16) of the K tile at `kb` (summed over kChains
+  // independent accumulators: a dependent chain of MMAs is latency bound).
+  __device__ static void qk_tile(uint32_t kb, int row0, const uint32_t (&qf)[NT][D / 16][2],
+                                 float (&out)[NT][4]) {
+    constexpr int KS = D / 16;
+    const int lane = threadIdx.x & 31, g8 = lane >> 2, t4 = lane & 3;
+    constexpr int kChains = C::kPair ? (NT == 1 ? 4 : 2) : (NT == 1 ? (KS < 8 ? KS : 8) : 2);
+    float sacc[kChains][NT][4];
+#pragma unroll
+    for (int c = 0; c < kChains; ++c)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sacc[c][nt][i] = 0.f;
+    // fp8 K straight into A fragments: lane (g8, t4) reads bytes [32*t4, +32) of rows g8 and
+    // g8 + 8 (two 16-byte chunks each, conflict-free under the swizzle) and widens dims
+    // 32*t4 + 4*ks + {0,1} / {2,3} to the k-pairs 2*t4 / 8 + 2*t4 of k-step ks.  The
+    // contraction over D is order-free; Q's fragments follow the same order.
+    uint32_t kw[F8 ? 2 : 1][F8 ? 8 : 1];
+    if constexpr (F8) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        uint32_t w0[4], w1[4];
+        lds_v4(kb + tile_off<C::kTS>(row0 + g8 + 8 * r, 2 * t4), w0);
+        lds_v4(kb + tile_off<C::kTS>(row0 + g8 + 8 * r, 2 * t4 + 1), w1);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          kw[r][i] = w0[i];
+          kw[r][4 + i] = w1[i];
+        }
+      }
+    }
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      if constexpr (F8) {
+        a0 = e4m3x2_to_f16x2(kw[0][ks] & 0xffffu);
+        a2 = e4m3x2_to_f16x2(kw[0][ks] >> 16);
+        a1 = e4m3x2_to_f16x2(kw[1][ks] & 0xffffu);
+        a3 = e4m3x2_to_f16x2(kw[1][ks] >> 16);
+      } else {
+        ldsm_x4(kb + tile_off<C::kTS>(row0 + (lane & 15), 2 * ks + (lane >> 4)), a0, a1, a2, a3);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        Mma<MT>::run(sacc[ks % kChains][nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
+    }
+#pragma unroll
+    for (int w = kChains / 2; w >= 1; w /= 2)
+#pragma unroll
+      for (int c = 0; c < w; ++c)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sacc[c][nt][i] += sacc[c + w][nt][i];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) out[nt][i] = sacc[0][nt][i];
+  }
+
+  // O^T += V^T P^T for rows [row0, row0 + 16) of the V tile at `vb`; rows past `valid` are
+  // zeroed in the fragments (their P is already zero, stale shared memory may not be).
+  __device__ static void pv_tile(uint32_t vb, int row0, int valid, const uint32_t (&pb)[NT][2],
+                                 float (&o)[D / 16][NT][4]) {
+    constexpr int KS = D / 16;
+    const int lane = threadIdx.x & 31, g8 = lane >> 2, t4 = lane & 3;
+    const bool partial = valid < 16;
+    const uint32_t mlo = (2 * t4 < valid ? 0x0000ffffu : 0u) | (2 * t4 + 1 < valid ? 0xffff0000u : 0u);
+    const uint32_t mhi = (2 * t4 + 8 < valid ? 0x0000ffffu : 0u) | (2 * t4 + 9 < valid ? 0xffff0000u : 0u);
+    // fp8 V: lane (g8, t4) holds dims [16*g8, +16) of token rows 2*t4, 2*t4 + 1, 2*t4 + 8,
+    // 2*t4 + 9 (one conflict-free 16-byte chunk each); m-tile mt's rows g8 and g8 + 8 are
+    // dims 16*g8 + 2*mt and +1 (the epilogue writes O in that order), and a byte permute
+    // pairs the two tokens of each k-pair before widening.
+    uint32_t vw[F8 ? 4 : 1][4];
+    if constexpr (F8) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) lds_v4(vb + tile_off<C::kTS>(row0 + 2 * t4 + (r & 1) + (r >> 1) * 8, g8), vw[r]);
+    }
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+      uint32_t a0, a1, a2, a3;
+      if constexpr (F8) {
+        const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
+        const uint32_t x = __byte_perm(vw[0][mt >> 1], vw[1][mt >> 1], sel);
+        const uint32_t y = __byte_perm(vw[2][mt >> 1], vw[3][mt >> 1], sel);
+        a0 = e4m3x2_to_f16x2(x & 0xffffu);
+        a1 = e4m3x2_to_f16x2(x >> 16);
+        a2 = e4m3x2_to_f16x2(y & 0xffffu);
+        a3 = e4m3x2_to_f16x2(y >> 16);
+      } else {
+        const int row = row0 + (lane & 7) + ((lane >> 4) << 3);
+        const int chunk = 2 * mt + ((lane >> 3) & 1);
+        ldsm_x4_t(vb + tile_off<C::kTS>(row, chunk), a0, a1, a2, a3);
+      }
+      if (partial) {
+        a0 &= mlo;
+        a1 &= mlo;
+        a2 &= mhi;
+        a3 &= mhi;
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) Mma<MT>::run(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
     }
   }
 
@@ -729,7 +812,7 @@ struct Kernel {
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int d = mt * 16 + g8 + (i >= 2 ? 8 : 0);
+          const int d = F8 ? 16 * g8 + 2 * mt + (i >= 2 ? 1 : 0) : mt * 16 + g8 + (i >= 2 ? 8 : 0);
           const int head = nt * 8 + 2 * t4 + (i & 1);
           red[(warp * C::kQRows + head) * C::kRedStride + d] = o[mt][nt][i];
         }
