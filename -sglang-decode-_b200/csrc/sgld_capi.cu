@@ -200,6 +200,14 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   const bool csr = d.indptr != nullptr;
   if (csr && d.page_size != 1) return fail(SGLD_ERR_INVALID_ARGUMENT, "CSR indexing uses page_size 1");
   if (!(d.scale == d.scale)) return fail(SGLD_ERR_INVALID_ARGUMENT, "scale is NaN");
+  const int32_t q_rows = d.q_rows == 0 ? geometry->batch_capacity : d.q_rows;
+  if (q_rows < 0 || q_rows > geometry->batch_capacity)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "q_rows must be 0 (capacity) or 1..batch_capacity");
+  const bool kv_write = d.new_loc != nullptr;
+  if (!kv_write && (d.k_new != nullptr || d.v_new != nullptr))
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "k_new / v_new need new_loc");
+  if (kv_write && (d.k_new == nullptr || d.v_new == nullptr))
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "the KV-cache write needs k_new, v_new and new_loc");
 
   sgld::DecodeLaunch a;
   std::memset(&a, 0, sizeof(a));
@@ -219,6 +227,7 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   a.kv_fp8 = kv_fp8 ? 1 : 0;
   if (a.d.k_scale == 0.f) a.d.k_scale = 1.f;
   if (a.d.v_scale == 0.f) a.d.v_scale = 1.f;
+  a.q_rows = q_rows;
   a.fast_kv = fast_kv ? 1 : 0;
   a.fast_q = (aligned16(d.q) && d.q_stride[2] == 1 && d.q_stride[0] % 8 == 0 && d.q_stride[1] % 8 == 0) ? 1 : 0;
   // Paged KV by tensor-map TMA: a box of 32 tokens never crosses a page because stages
@@ -238,7 +247,31 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
     }
   }
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = sgld::launch_decode(a, st);
+  cudaError_t e;
+  if (kv_write) {   // the step's KV-cache write, chained right before the decode
+    sgld::KVWrite kw = {};
+    kw.k_new = d.k_new;
+    kw.v_new = d.v_new;
+    kw.new_loc = d.new_loc;
+    kw.k = const_cast<void*>(d.k);
+    kw.v = const_cast<void*>(d.v);
+    for (int i = 0; i < 4; ++i) kw.k_stride[i] = a.d.k_stride[i], kw.v_stride[i] = a.d.v_stride[i];
+    for (int i = 0; i < 3; ++i) kw.kn_stride[i] = d.knew_stride[i], kw.vn_stride[i] = d.vnew_stride[i];
+    kw.slots = d.kv_extent > 0 ? d.kv_extent * ps : 0;
+    kw.rows = q_rows;
+    kw.page_size = ps;
+    kw.kv_heads = d.kv_heads;
+    kw.head_dim = d.head_dim;
+    kw.loc_int32 = d.new_loc_int32 != 0 ? 1 : 0;
+    kw.dtype = d.dtype;
+    kw.pool_fp8 = kv_fp8 ? 1 : 0;
+    kw.k_scale = a.d.k_scale;
+    kw.v_scale = a.d.v_scale;
+    kw.status = d.status;
+    e = sgld::launch_kv_write(kw, st, true);
+    if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent KV-cache write launch");
+  }
+  e = sgld::launch_decode(a, st);
   if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent launch");
   e = sgld::launch_merge(d.partial, d.lse, plan->counts, plan->error, d.out, d.dtype, geometry->batch_capacity,
                          d.query_heads, d.head_dim, geometry->max_splits, st, true);

@@ -41,7 +41,30 @@ struct alignas(64) DecodeLaunch {
   int32_t kv_fp8;    // K/V are e4m3 (Q and the output are fp16/bf16)
   int32_t tma_kv;    // paged KV loaded by tensor-map TMA boxes of box_rows tokens
   int32_t box_rows;
+  int32_t q_rows;    // rows of q (requests at or past it read a zero query, status bit 64)
 };
+
+// KV-cache write launched right before the decode of the same call (SGLang's
+// set_kv_buffer): row (r, head) of k_new / v_new goes to token slot new_loc[r].
+struct KVWrite {
+  const void* k_new;
+  const void* v_new;
+  const void* new_loc;
+  void* k;
+  void* v;
+  int64_t k_stride[4], v_stride[4];   // pool strides (page, token-in-page, head, dim)
+  int64_t kn_stride[3], vn_stride[3]; // new-row strides (request, head, dim)
+  int64_t slots;                      // token slots in the pool (0: unchecked)
+  int32_t rows, page_size, kv_heads, head_dim, loc_int32;
+  int32_t dtype;                      // of k_new / v_new (SGLD_DTYPE_F16 / BF16)
+  int32_t pool_fp8;                   // pool holds e4m3: store e4m3(x / scale), saturating
+  float k_scale, v_scale;
+  int32_t* status;
+};
+
+// programmatic: launch as a programmatic dependent of the preceding kernel (PDL); the
+// kernel still waits for that kernel (which may have produced k_new / v_new) to finish.
+cudaError_t launch_kv_write(const KVWrite& kv, cudaStream_t stream, bool programmatic);
 
 cudaError_t launch_decode(const DecodeLaunch& a, cudaStream_t stream);
 

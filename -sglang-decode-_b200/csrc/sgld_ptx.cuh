@@ -91,6 +91,11 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
       : "memory");
 }
 
+// Bring `bytes` at `src` into L2 ahead of use (16-byte aligned address, size a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Tiled tensor-map copy of a 4D box (coordinates innermost first) into shared memory.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2, int c3,
                                             uint64_t* bar) {

@@ -42,6 +42,10 @@ class DecodeArgs(ctypes.Structure):
         ("dtype", ctypes.c_int32), ("query_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
         ("head_dim", ctypes.c_int32), ("page_size", ctypes.c_int32), ("scale", ctypes.c_float), ("logit_cap", ctypes.c_float),
         ("kv_dtype", ctypes.c_int32), ("k_scale", ctypes.c_float), ("v_scale", ctypes.c_float),
+        ("q_rows", ctypes.c_int32),
+        ("k_new", ctypes.c_void_p), ("v_new", ctypes.c_void_p), ("new_loc", ctypes.c_void_p),
+        ("knew_stride", ctypes.c_int64 * 3), ("vnew_stride", ctypes.c_int64 * 3),
+        ("new_loc_int32", ctypes.c_int32),
         ("counter", ctypes.c_void_p), ("partial", ctypes.c_void_p), ("lse", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
     ]
@@ -51,7 +55,7 @@ DTYPE_F16, DTYPE_BF16, DTYPE_E4M3 = 0, 1, 2
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error"}
 EXPORTS = ("sgld_abi_version", "sgld_last_error", "sgld_layer_workspace_bytes", "sgld_plan_build",
            "sgld_decode_persistent", "sgld_merge_splits")
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 _lock = threading.Lock()
 _lib = None

@@ -5,8 +5,12 @@ the model-runner import patch selects this subclass; unsupported model geometry,
 speculative modes, sliding windows and capacity overflow keep the original decode.  The decode itself runs on the B200 engine (one plan build per
 step, one fused decode launch per layer over SGLang's CSR kv_indptr/kv_indices).
 Differences from the reference: any integer GQA group 1..16 is eligible (Qwen2-7B's
-group of 7 included), so only groups above 16 fall back; and layers with a logit soft
-cap (``layer.logit_cap > 0``) run on the engine with that cap instead of falling back.
+group of 7 included), so only groups above 16 fall back; layers with a logit soft
+cap (``layer.logit_cap > 0``) run on the engine with that cap instead of falling back;
+and the steps around the decode are folded into the engine call: the new token's K/V
+are written to the pool by a kernel chained right before the decode (instead of
+``set_kv_buffer``'s launches, reference ``sglang_backend.py:91-92``) and Q is read where
+the model left it (no per-layer copy into a capacity-sized buffer, reference ``:102-103``).
 """
 import os
 
@@ -53,7 +57,6 @@ class ScheduledTritonBackend(TritonAttnBackend):
         # Indexed by absolute layer_id; pipeline parallel partitions may leave gaps.
         layers = c.hf_config.num_hidden_layers
         self.scheduled = DecodeEngine(config, self.device, key.dtype, layers, rules, force)
-        self.query_buffers = [torch.empty_like(x.output) for x in self.scheduled.layers]
 
     def _begin_step(self, bs, decode, spec_info):
         self._prepared = False
@@ -95,8 +98,6 @@ class ScheduledTritonBackend(TritonAttnBackend):
                 or layer.v_head_dim != engine.config.head_dim
                 or getattr(layer, "sliding_window_size", -1) not in (None, -1)):
             return super().forward_decode(q, k, v, layer, forward_batch, save_kv_cache)
-        if save_kv_cache:
-            forward_batch.token_to_kv_pool.set_kv_buffer(layer, forward_batch.out_cache_loc, k, v)
         meta, p = self.forward_metadata, engine.plan
         batch = q.shape[0]
         if not self._prepared or not self.reuse_plan:
@@ -106,11 +107,15 @@ class ScheduledTritonBackend(TritonAttnBackend):
             p.splits[:batch].copy_(meta.num_kv_splits[:batch])
             engine.prepare()
             self._prepared = True
-        qbuf = self.query_buffers[layer.layer_id]
-        qbuf[:batch].copy_(q.view(batch, engine.config.query_heads, engine.config.head_dim))
+        c = engine.config
+        fused = {}
+        if save_kv_cache:
+            # Row r of k/v is stored at out_cache_loc[r] right before the decode reads the pool.
+            fused = dict(k_new=k.view(batch, c.kv_heads, c.head_dim), v_new=v.view(batch, c.kv_heads, c.head_dim),
+                         new_loc=forward_batch.out_cache_loc)
         out = engine.execute(
-            qbuf, forward_batch.token_to_kv_pool.get_key_buffer(layer.layer_id),
+            q.view(batch, c.query_heads, c.head_dim), forward_batch.token_to_kv_pool.get_key_buffer(layer.layer_id),
             forward_batch.token_to_kv_pool.get_value_buffer(layer.layer_id), meta.kv_indices,
             layer=layer.layer_id, indptr=meta.kv_indptr, scale=layer.scaling,
-            logit_cap=max(0.0, float(layer.logit_cap or 0.0)))
+            logit_cap=max(0.0, float(layer.logit_cap or 0.0)), **fused)
         return out[:batch].view(batch, -1)

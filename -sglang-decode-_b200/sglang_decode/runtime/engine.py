@@ -50,7 +50,7 @@ class DecodeEngine:
         build_plan(self.plan, self.force_mode)
 
     def execute(self, q, k, v, pages, layer=0, *, indptr=None, scale=None, logit_cap=0.0,
-                k_scale=1.0, v_scale=1.0):
+                k_scale=1.0, v_scale=1.0, k_new=None, v_new=None, new_loc=None):
         """KV layout: [pages,page_size,kv_heads,D], or CSR [tokens,kv_heads,D].
 
         Metadata and Q/KV must be ready on the current CUDA stream. Fixed buffers
@@ -59,6 +59,17 @@ class DecodeEngine:
         does for models such as Gemma-2 (an addition: the reference has no capped path).
         K/V may be fp8 (``torch.float8_e4m3fn``, head_dim 128) with a fp16/bf16 Q: scores
         then use ``k_scale * k`` and the output ``v_scale * v`` (also an addition).
+
+        Additions for the SGLang step around the decode (the reference copies Q into a
+        capacity-sized buffer and calls ``set_kv_buffer`` first):
+
+        * Q may have fewer rows than the capacity (any strides); the plan's active count
+          must not exceed ``q.shape[0]`` (a task past it reads zeros and sets status 64).
+        * ``k_new``/``v_new`` ([q rows, kv_heads, D], Q's dtype, any strides) with
+          ``new_loc`` ([q rows] int64 or int32 token slots) add the KV-cache write to the
+          call: row r is stored at slot ``new_loc[r]`` (an fp8 pool stores
+          ``e4m3(x / k_scale)``, saturating) by a kernel chained right before the decode,
+          so the result equals ``set_kv_buffer`` followed by the decode.
         """
         c, p, out = self.config, self.plan, self.layers[layer]
         kv_fp8 = k.dtype == _FP8
@@ -66,8 +77,9 @@ class DecodeEngine:
             raise ValueError("BF16/FP16 Q/K/V of identical dtype are required (or fp8 e4m3 K/V)")
         if kv_fp8 and c.head_dim != 128:
             raise ValueError("fp8 K/V are supported for head_dim 128")
-        if tuple(q.shape) != (c.batch_capacity, c.query_heads, c.head_dim):
-            raise ValueError("Q must use the capture capacity; pad inactive rows")
+        if (q.ndim != 3 or tuple(q.shape[1:]) != (c.query_heads, c.head_dim)
+                or not 1 <= q.shape[0] <= c.batch_capacity):
+            raise ValueError("Q must be [rows <= capacity, query_heads, head_dim]")
         if out.output.dtype != q.dtype:
             raise ValueError("Q dtype differs from the engine's output dtype")
         for t in (q, k, v, pages):
@@ -118,6 +130,25 @@ class DecodeEngine:
         if not cap >= 0.0 or cap == float("inf"):
             raise ValueError("logit_cap must be a finite value >= 0 (0 disables it)")
         a.logit_cap = cap
+        a.q_rows = q.shape[0]
+        if new_loc is None:
+            if k_new is not None or v_new is not None:
+                raise ValueError("k_new / v_new need new_loc")
+            a.k_new = a.v_new = a.new_loc = None
+        else:
+            rows = q.shape[0]
+            for t in (k_new, v_new):
+                if (t is None or t.dtype != q.dtype or t.device != p.device
+                        or tuple(t.shape) != (rows, c.kv_heads, c.head_dim)):
+                    raise ValueError("k_new / v_new must be [q rows, kv_heads, head_dim] in Q's dtype")
+            if (new_loc.dtype not in (torch.int64, torch.int32) or new_loc.device != p.device
+                    or new_loc.ndim != 1 or new_loc.shape[0] != rows or new_loc.stride(0) != 1):
+                raise ValueError("new_loc must be a contiguous 1-D int64/int32 tensor, one slot per Q row")
+            a.k_new, a.v_new = k_new.data_ptr(), v_new.data_ptr()
+            a.knew_stride[:] = k_new.stride()
+            a.vnew_stride[:] = v_new.stride()
+            a.new_loc = new_loc.data_ptr()
+            a.new_loc_int32 = 1 if new_loc.dtype == torch.int32 else 0
         a.counter, a.partial, a.lse = out.counter.data_ptr(), out.partial.data_ptr(), out.lse.data_ptr()
         a.status = out.status.data_ptr()
         stream = torch.cuda.current_stream(p.device).cuda_stream

@@ -56,6 +56,10 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--kv-dtype", choices=["q", "fp8"], default="q",
                     help="K/V pool dtype: the Q dtype (the reference's), or e4m3 with unit scales")
+    ap.add_argument("--kv-write", choices=["none", "separate", "fused"], default="none",
+                    help="time SGLang's decode step with the new token's K/V write: 'separate' = "
+                         "set_kv_buffer (two index_put launches) + Q copy + decode, as the reference "
+                         "adapter does; 'fused' = the single decode launch that stores the rows itself")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -279,8 +283,33 @@ def run_ours(args):
         del data
         torch.cuda.empty_cache()
 
+    kv_write = getattr(args, "kv_write", "none")
+    if kv_write != "none":
+        if fp8:
+            raise SystemExit("--kv-write needs a 16-bit KV pool")
+        rows = len(b.lengths)
+        gen = torch.Generator(device=device).manual_seed(23)
+        k_new = torch.randn(rows, hkv, c.head_dim, generator=gen, device=device, dtype=b.dtype)
+        v_new = torch.randn(rows, hkv, c.head_dim, generator=gen, device=device, dtype=b.dtype)
+        q_in = q[:rows].clone()                      # the model's Q for this step
+        if indptr is not None:                       # each request's newest slot
+            new_loc = pages[indptr[1:rows + 1].long() - 1].long()
+        else:
+            last = torch.tensor([n - 1 for n in b.lengths], device=device)
+            new_loc = (pages[torch.arange(rows, device=device), last // c.page_size].long() * c.page_size
+                       + last % c.page_size)
+        flat_k, flat_v = k.view(-1, hkv, c.head_dim), v.view(-1, hkv, c.head_dim)
+        q_buf = torch.zeros_like(q)
+
     def step():
         engine.prepare()
+        if kv_write == "separate":
+            flat_k[new_loc] = k_new
+            flat_v[new_loc] = v_new
+            q_buf[:rows].copy_(q_in)
+            return engine.execute(q_buf, k, v, pages, indptr=indptr)
+        if kv_write == "fused":
+            return engine.execute(q_in, k, v, pages, indptr=indptr, k_new=k_new, v_new=v_new, new_loc=new_loc)
         return engine.execute(q, k, v, pages, indptr=indptr)
 
     for _ in range(args.warmup):
@@ -305,6 +334,11 @@ def run_ours(args):
         torch.cuda.synchronize()
         start.record(stream)
         for i in range(args.steps):
+            if kv_write != "none":                   # the whole step is the decode here
+                dec_events[i][0].record(stream)
+                step()
+                dec_events[i][1].record(stream)
+                continue
             engine.prepare()
             dec_events[i][0].record(stream)
             engine.execute(q, k, v, pages, indptr=indptr)
@@ -390,7 +424,7 @@ def run_ours(args):
                        "mode": "AUTO" if args.mode < 0 else args.mode,
                        "policy": Path(args.policy).name if args.policy else None,
                        "heads_per_gpu": {"kv": hkv, "q": hq}, "workers": sms,
-                       "l2": "not flushed: KV pool per GPU > 126 MB L2"},
+                       "l2": "not flushed: KV pool per GPU > 126 MB L2", "kv_write": kv_write},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_source": peak_kind,

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define SGLD_ABI_VERSION 5
+#define SGLD_ABI_VERSION 6
 
 typedef enum sgld_status {
   SGLD_OK = 0,
@@ -121,16 +121,35 @@ typedef struct sgld_decode_args {
                            fp16/bf16 q; head_dim 128).  The reference has no fp8 path      */
   float k_scale;        /* scores use k_scale * k (0 reads as 1): dequantises fp8 keys      */
   float v_scale;        /* outputs use v_scale * v (0 reads as 1)                           */
+  int32_t q_rows;       /* rows of q (and of k_new / v_new / new_loc); 0 means batch_capacity.
+                           The plan's active count must not exceed it: a task of a request at
+                           or past q_rows reads a zero query and sets status bit 64          */
+  /* KV-cache write: SGLang's set_kv_buffer, the step before the decode (reference
+     integrations/sglang_backend.py:91-92), chained into this call.  With new_loc
+     non-NULL, row r < q_rows of k_new / v_new ([q_rows, Hkv, D] in `dtype`, any strides)
+     is stored at token slot new_loc[r] of k / v (paged: page new_loc/page_size, row
+     new_loc%page_size) before the decode reads the pool, so the result is exactly the
+     write followed by the decode.  An e4m3 pool stores e4m3(x / k_scale) (v: v_scale),
+     rounded to nearest even and saturated to +-448.  A slot outside kv_extent is
+     skipped and sets status bit 128.                                                     */
+  const void* k_new;
+  const void* v_new;
+  const void* new_loc;  /* [q_rows] int64, or int32 when new_loc_int32 != 0                 */
+  int64_t knew_stride[3];  /* elements: (request, head, dim)                               */
+  int64_t vnew_stride[3];
+  int32_t new_loc_int32;
   /* Layer scratch -- reference runtime/workspace.py:26-40 (LayerBuffers) */
   int32_t* counter;     /* [2]  claim counter + exit ticket; zero before, left zero after    */
   float* partial;       /* [B, Hq, Smax, D] fp32 normalised split outputs, 16-byte aligned   */
   float* lse;           /* [B, Hq, Smax]    fp32 natural-log LSE per split                   */
-  int32_t* status;      /* [1]  0 = ok; bounded in-kernel wait expired otherwise (sticky)    */
+  int32_t* status;      /* [1]  0 = ok; otherwise sticky error bits: 1-32 a bounded in-kernel
+                           wait expired, 64 q_rows too small, 128 a new_loc slot out of range */
 } sgld_decode_args;
 
 /*
  * Persistent paged GQA decode followed by the split merge (two launches: W decode
- * CTAs, then the merge grid as a programmatic dependent launch).
+ * CTAs, then the merge grid as a programmatic dependent launch; with new_loc set, the
+ * KV-cache write is a third launch chained right before the decode).
  * Replaces reference runtime/engine.py:62-73: the counter reset, the
  * persistent_decode launch (kernels/attention.py:87-130, task body :12-84) and
  * the merge_splits launch (kernels/merge.py:7-30).  Task dispatch follows

@@ -93,6 +93,15 @@ def test_host_checks_reject_bad_arguments_without_touching_a_gpu(lib):
     assert b"head dimensions" in lib.sgld_last_error()
     args.head_dim, args.query_heads = 128, 8 * 17
     assert lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None) == 2
+    # q_rows and the fused KV write (every case below fails its host check before a launch)
+    args.query_heads = 32
+    decode = lambda: lib.sgld_decode_persistent(ctypes.byref(args), ctypes.byref(plan), ctypes.byref(geo), None)
+    args.q_rows = 65                                            # more Q rows than the capacity (64)
+    assert decode() == 1 and b"q_rows" in lib.sgld_last_error()
+    args.q_rows, args.k_new = 0, 16                             # new rows without their slots
+    assert decode() == 1 and b"new_loc" in lib.sgld_last_error()
+    args.new_loc = 16                                           # slots without v_new
+    assert decode() == 1 and b"k_new, v_new and new_loc" in lib.sgld_last_error()
     with pytest.raises(ValueError):
         _native.check(1, "probe")
 
@@ -109,7 +118,10 @@ int main(void) {
   F(sgld_plan_geometry, workers) F(sgld_plan_buffers, static_next)
   F(sgld_decode_args, q_stride) F(sgld_decode_args, kv_extent) F(sgld_decode_args, dtype)
   F(sgld_decode_args, scale) F(sgld_decode_args, logit_cap) F(sgld_decode_args, kv_dtype)
-  F(sgld_decode_args, k_scale) F(sgld_decode_args, v_scale) F(sgld_decode_args, counter) F(sgld_decode_args, partial)
+  F(sgld_decode_args, k_scale) F(sgld_decode_args, v_scale) F(sgld_decode_args, q_rows)
+  F(sgld_decode_args, k_new) F(sgld_decode_args, v_new) F(sgld_decode_args, new_loc)
+  F(sgld_decode_args, knew_stride) F(sgld_decode_args, vnew_stride) F(sgld_decode_args, new_loc_int32)
+  F(sgld_decode_args, counter) F(sgld_decode_args, partial)
   F(sgld_decode_args, lse) F(sgld_decode_args, status)
   return 0;
 }
@@ -131,6 +143,7 @@ def test_ctypes_structs_match_the_c_header(tmp_path):
         "sgld_plan_buffers.static_next": _native.PlanBuffersC.static_next.offset,
     }
     for field in ("q_stride", "kv_extent", "dtype", "scale", "logit_cap", "kv_dtype", "k_scale", "v_scale",
+                  "q_rows", "k_new", "v_new", "new_loc", "knew_stride", "vnew_stride", "new_loc_int32",
                   "counter", "partial", "lse", "status"):
         want[f"sgld_decode_args.{field}"] = getattr(_native.DecodeArgs, field).offset
     assert {k: int(v) for k, v in got.items()} == want

@@ -147,12 +147,41 @@ def test_adapter_decode_matches_oracle_and_builds_one_plan_per_step(adapter, que
         out = backend.forward_decode(q, k, v, layer, fb)
         torch.cuda.synchronize()
         assert out.shape == (len(lengths), query_heads * 128)
-        # the new token's K/V were written before the decode read them
+        # the launch itself stored the new token's K/V (no set_kv_buffer call) and the
+        # decode saw them: the oracle reads the updated pool
+        pool = runner.token_to_kv_pool
+        assert torch.equal(pool.k[layer_id][fb.out_cache_loc.long()], k)
+        assert torch.equal(pool.v[layer_id][fb.out_cache_loc.long()], v)
+        _check(out, _oracle(backend, runner, fb, layer, q))
+    assert backend.fallback_calls == 0
+    assert runner.token_to_kv_pool.writes == 0, "the KV write is fused into the decode launch"
+    assert prepares["n"] == 1, "the plan is built once per step and reused by every layer"
+    assert backend.scheduled.layers[0].status.item() == 0
+
+
+@pytest.mark.gpu
+def test_adapter_reads_q_k_v_in_place_from_the_projection_output(adapter, cuda_device):
+    """q, k, v as SGLang passes them: views of one QKV projection output (q flat
+    [bs, Hq*D], k/v [bs, Hkv, D]); no per-layer Q copy, the pool written by the launch."""
+    runner = _runner(28, 4)
+    backend = adapter.ScheduledTritonBackend(runner)
+    lengths = [5, 700, 64, 1500]
+    fb = _batch(runner, lengths, seed=8)
+    backend.init_forward_metadata(fb)
+    g = torch.Generator(device="cuda").manual_seed(12)
+    bs, hq, hkv, d = len(lengths), 28, 4, 128
+    for layer_id in range(2):
+        layer = F.FakeLayer.make(layer_id, hq, hkv, d)
+        qkv = torch.randn(bs, (hq + 2 * hkv) * d, generator=g, device="cuda", dtype=torch.bfloat16)
+        q = qkv[:, :hq * d]
+        k = qkv[:, hq * d:(hq + hkv) * d].view(bs, hkv, d)
+        v = qkv[:, (hq + hkv) * d:].view(bs, hkv, d)
+        out = backend.forward_decode(q, k, v, layer, fb)
+        torch.cuda.synchronize()
         pool = runner.token_to_kv_pool
         assert torch.equal(pool.k[layer_id][fb.out_cache_loc.long()], k)
         _check(out, _oracle(backend, runner, fb, layer, q))
-    assert backend.fallback_calls == 0
-    assert prepares["n"] == 1, "the plan is built once per step and reused by every layer"
+    assert backend.fallback_calls == 0 and runner.token_to_kv_pool.writes == 0
     assert backend.scheduled.layers[0].status.item() == 0
 
 
