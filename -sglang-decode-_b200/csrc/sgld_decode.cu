@@ -21,11 +21,13 @@
 //        per instruction); CSR and other layouts move by 16-byte cp.async spread over
 //        the P warps (the issue rate of one warp caps its bandwidth).
 //        Producer 0 also loads each task's query group into a double-buffered Q slot.
-//   consumers (4 warps)  each take 16 tokens of a stage.  QK and PV run on tensor
+//   consumers (4 or 8 warps)  each take 16 tokens of a stage, a task's stages two at a time
+//        where the ring allows (one softmax update per 32 tokens); the fp8 kernel runs two
+//        quads of 4 that take alternate iterations of a task.  QK and PV run on tensor
 //        cores (mma.sync m16n8k16) in "swapped" form so the GQA group (padded to 8 or
 //        16) is the N dimension: S^T = K Q^T and O^T += V^T P^T; movmatrix turns the
 //        score accumulator into the P^T operand.  FP32 online softmax state is
-//        warp-private; at the end of a task the four warp states are combined and
+//        warp-private; at the end of a task the warp states are combined and
 //        the normalised partial and natural-log LSE of every query head of the group
 //        are stored to slot (request*Hq + head)*Smax + split (attention.py:81-84).
 //
@@ -67,12 +69,20 @@ struct TaskDesc {
 template <int D, int NT, bool F8 = false>
 struct Cfg {
   static constexpr bool kBig = D * NT >= 512;            // D=256 with a 16-row group
-  static constexpr int kConsumerWarps = 4;
+  // Consumer quads: four warps each take 16 rows of a stage.  A single quad is one
+  // latency-bound warp per SM sub-partition.  The fp8 kernel (group <= 8), whose consumers
+  // also widen every K/V byte, runs two quads that take alternate iterations of a task
+  // (measured on B200: C3 946 -> 758 us).  The 16-bit kernels stay at one quad: with two,
+  // they lose the paired stages (the ring has no stage to spare) and ran 5% slower.
+  static constexpr int kQuads = (F8 && NT == 1) ? 2 : 1;
+  static constexpr int kConsumerWarps = 4 * kQuads;
   // One warp's cp.async issue rate caps its bandwidth, so the copies are spread over
   // as many producer warps as the register file allows next to the consumers (16 warps
   // at 128 registers for D <= 128 and a group of at most 8).  With tensor-map copies
   // producer 0 works alone.
-  static constexpr int kProducerWarps = kBig ? 2 : (NT == 2 ? 5 : (D >= 256 ? 6 : 10));
+  // fp8 stages carry half the bytes: 6 producers keep the CTA at 16 warps (at most four per
+  // SM sub-partition), hence 128 registers a thread for the widening consumers.
+  static constexpr int kProducerWarps = kBig ? 2 : (NT == 2 ? 5 : (D >= 256 ? 6 : (F8 ? 6 : 10)));
   static constexpr int kProducerWarp0 = kConsumerWarps;
   static constexpr int kIndexerWarp = kProducerWarp0 + kProducerWarps;
   static constexpr int kSchedulerWarp = kIndexerWarp + 1;
@@ -99,13 +109,15 @@ struct Cfg {
   static constexpr int kSDBytes = kSD * kSDEntry;
   static constexpr int kMiscBytes = 4096;
   static constexpr int kFixed1 = 2 * kQBytes + kSDBytes + kMiscBytes;
-  static constexpr int kRedBufs = (kFixed1 + 2 * kRedOne + 3 * kStageBytes <= kSmemBudget) ? 2 : 1;
+  // Double-buffered reduction when it leaves enough stages (two quads hold two stages).
+  static constexpr int kRedBufs = (kFixed1 + 2 * kRedOne + (kQuads == 2 ? 5 : 3) * kStageBytes <= kSmemBudget) ? 2 : 1;
   static constexpr int kFixed = kFixed1 + kRedBufs * kRedOne;
   static constexpr int kStagesRaw = (kSmemBudget - kFixed) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-  // Consumers hold two stages at a time (paired stages) when the ring is deep enough; the
-  // 16-row-group kernels have no registers to spare for the second sub-tile.
-  static constexpr bool kPair = kStages >= 4 && NT == 1;
+  // Consumers hold two stages at a time (paired stages) when the ring is deep enough (each
+  // quad holds two and as many stay in flight); the 16-row-group kernels have no registers
+  // to spare for the second sub-tile.
+  static constexpr bool kPair = kStages >= 4 * kQuads && NT == 1;
   static_assert(kStages >= 2, "shared memory budget too small");
   // Offsets from the 1024-byte aligned base (tiles first: they need the alignment).
   static constexpr int kOffQ = kStages * kStageBytes;
@@ -126,7 +138,7 @@ struct Misc {
   StageHdr hdr[8];
   StageHdr shdr[12];
   TaskDesc tq[4];
-  float m[2][4][16], l[2][4][16];
+  float m[2][8][16], l[2][8][16];   // per consumer warp (up to two quads)
 };
 
 // Byte offset of 16-byte chunk `chunk` of row `row` in a tile of ROWS rows laid out
@@ -541,6 +553,7 @@ struct Kernel {
   __device__ static void consumer(const DecodeLaunch& a, unsigned char* smem, Misc& ms) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g8 = lane >> 2, t4 = lane & 3;
+    const int quad = warp >> 2;   // with two quads, quad q takes iterations q, q+2, ... of each task
     // Scores go to the log2 domain.  With a soft cap (logit_cap > 0) the scaled score s
     // becomes cap * tanh(s / cap) first; tanh comes from 1 - 2 / (2^(2x log2 e) + 1), exact at
     // both saturations (2^big = inf gives 1, 2^-big = 0 gives -1).
@@ -555,7 +568,7 @@ struct Kernel {
     float o[KS][NT][4];
     float m[NT][2], lsum[NT][2];
 
-    int s = 0, task_idx = 0;
+    int s = 0, task_idx = 0, titer = 0;
     uint32_t ph = 0;
     while (true) {
       if (!warp_wait(&ms.full[s], ph, status, kStatusWaitFull)) return;
@@ -563,6 +576,7 @@ struct Kernel {
       if (h.flags & kFlagExit) break;
       unsigned char* stage = smem + s * C::kStageBytes;
       if (h.flags & kFlagFirst) {
+        titer = 0;
         const int qs = task_idx & 1;
         if (!warp_wait(&ms.qfull[qs], (task_idx >> 1) & 1, status, kStatusWaitQ)) return;
         const uint32_t qbase = smem_addr(smem + C::kOffQ + qs * C::kQBytes);
@@ -603,7 +617,11 @@ struct Kernel {
       // task's next stage; the warp takes its 16 rows of both, so one softmax update, one O
       // rescale and one set of shuffles cover 32 tokens and the two sub-tiles' MMAs overlap.
       // Pairs restart at every task, so the arithmetic does not depend on the dispatch mode.
-      const int row0 = warp * 16;
+      // Every warp reads every stage header (the task boundaries); the owning quad computes.
+      // Ownership counts iterations (a stage or a pair) from the task's first stage, so it
+      // does not depend on the dispatch mode.
+      const bool own = C::kQuads == 1 || titer % C::kQuads == quad;
+      const int row0 = (warp & 3) * 16;
       const bool pair = C::kPair && !(h.flags & kFlagLast);
       int s2 = s + 1;
       uint32_t ph2 = ph;
@@ -619,7 +637,7 @@ struct Kernel {
       }
       const int valid_a = h.ntok - row0;            // live tokens of this warp's rows in each
       const int valid_b = pair ? ntok2 - row0 : 0;  // stage (a non-last stage is full)
-      if (valid_a > 0) {
+      if (own && valid_a > 0) {
         const uint32_t ka = smem_addr(stage), kb2 = smem_addr(smem + s2 * C::kStageBytes);
         const bool has_b = valid_b > 0;
         float sv[2][NT][4];
@@ -682,6 +700,7 @@ struct Kernel {
         if (!epilogue(a, smem, ms, h, task_idx, o, m, lsum)) return;
         ++task_idx;
       }
+      ++titer;
       if (pair) {
         s = s2;
         ph = ph2;
