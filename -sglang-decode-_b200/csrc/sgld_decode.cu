@@ -818,7 +818,7 @@ struct Kernel {
     }
   }
 
-  // Combine the four warps' (m, l, O) of one task and store the normalised partial and
+  // Combine the consumer warps' (m, l, O) of one task and store the normalised partial and
   // natural-log LSE of every query head of the group.
   __device__ static bool epilogue(const DecodeLaunch& a, unsigned char* smem, Misc& ms, const StageHdr& h,
                                   int task_idx, float (&o)[D / 16][NT][4], float (&m)[NT][2],
