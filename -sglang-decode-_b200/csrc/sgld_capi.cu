@@ -167,8 +167,14 @@ int sgld_plan_build(const sgld_plan_buffers* plan, const sgld_plan_geometry* geo
   return SGLD_OK;
 }
 
-int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers* plan,
-                           const sgld_plan_geometry* geometry, void* stream) {
+}  // extern "C"
+
+namespace sgld {
+
+// Every host-side check of sgld_decode_persistent, with nothing enqueued: shapes, dtypes,
+// pointers (scratch included), strides and capacities.  SGLD_OK when a launch may follow.
+int validate_decode(const sgld_decode_args* args, const sgld_plan_buffers* plan,
+                    const sgld_plan_geometry* geometry) {
   if (args == nullptr) return fail(SGLD_ERR_INVALID_ARGUMENT, "decode args are NULL");
   int rc = check_geometry(geometry);
   if (rc) return rc;
@@ -209,6 +215,41 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   if (kv_write && (d.k_new == nullptr || d.v_new == nullptr))
     return fail(SGLD_ERR_INVALID_ARGUMENT, "the KV-cache write needs k_new, v_new and new_loc");
 
+  return SGLD_OK;
+}
+
+// The calling thread's current CUDA context (a CUcontext), or nullptr when the driver
+// entry point is unavailable.  Caches keyed by device ordinal compare it to notice a
+// device reset (a new primary context reuses the ordinal but not the old addresses).
+void* current_context() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  static GetCurrent fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<GetCurrent>(nullptr);
+    return reinterpret_cast<GetCurrent>(p);
+  }();
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
+
+}  // namespace sgld
+
+extern "C" {
+
+int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers* plan,
+                           const sgld_plan_geometry* geometry, void* stream) {
+  int rc = sgld::validate_decode(args, plan, geometry);
+  if (rc) return rc;
+  const sgld_decode_args& d = *args;
+  const bool kv_fp8 = d.kv_dtype == SGLD_DTYPE_E4M3;
+  const int group = d.query_heads / d.kv_heads;
+  const bool csr = d.indptr != nullptr;
+  const int32_t q_rows = d.q_rows == 0 ? geometry->batch_capacity : d.q_rows;
+  const bool kv_write = d.new_loc != nullptr;
   sgld::DecodeLaunch a;
   std::memset(&a, 0, sizeof(a));
   a.d = d;

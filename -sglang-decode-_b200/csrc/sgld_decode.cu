@@ -41,6 +41,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <type_traits>
 
 #include "sgld_internal.cuh"
@@ -964,16 +965,20 @@ template <typename T, int D, int NT, bool F8>
 cudaError_t launch_typed(const DecodeLaunch& a, cudaStream_t stream) {
   using C = Cfg<D, NT, F8>;
   constexpr int kMaxDevices = 64;
-  static bool configured[kMaxDevices] = {};   // the smem attribute is per device
+  // The shared-memory attribute belongs to the device's context: remember the context it
+  // was set in (a device reset creates a new one).  Host threads may race here; setting
+  // the attribute twice is harmless.
+  static std::atomic<void*> configured[kMaxDevices] = {};
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return e;
   if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
-  if (!configured[device]) {
+  void* ctx = current_context();
+  if (ctx == nullptr || configured[device].load(std::memory_order_acquire) != ctx) {
     e = cudaFuncSetAttribute(decode_kernel<T, D, NT, F8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmemBytes);
     if (e != cudaSuccess) return e;
-    configured[device] = true;
+    configured[device].store(ctx, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.workers);

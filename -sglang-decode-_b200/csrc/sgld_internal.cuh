@@ -71,6 +71,14 @@ cudaError_t launch_decode(const DecodeLaunch& a, cudaStream_t stream);
 // Record `msg` as the calling host thread's sgld_last_error() message; returns `code`.
 int set_last_error(int code, const char* msg);
 
+// Every host-side check of sgld_decode_persistent (nothing is enqueued); SGLD_OK or the
+// status that call would return, with sgld_last_error() set.
+int validate_decode(const sgld_decode_args* args, const sgld_plan_buffers* plan,
+                    const sgld_plan_geometry* geometry);
+
+// The calling thread's current CUDA context (a CUcontext), nullptr if unknown.
+void* current_context();
+
 // programmatic: launch as a programmatic dependent of the preceding kernel (PDL).
 cudaError_t launch_merge(const float* partial, const float* lse, const int32_t* counts,
                          const int32_t* error, void* out, int32_t dtype, int32_t bcap, int32_t hq,

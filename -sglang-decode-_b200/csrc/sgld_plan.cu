@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
 
 cudaError_t launch_plan(const PlanLaunch& a, cudaStream_t stream) {
   constexpr int kMaxDevices = 64;
-  static bool configured[kMaxDevices] = {};
+  static void* configured[kMaxDevices] = {};   // context the smem attribute was set in
   static std::mutex mu;
   const int smem = static_cast<int>(sizeof(PlanShared));
   int device = 0;
@@ -629,10 +629,11 @@ cudaError_t launch_plan(const PlanLaunch& a, cudaStream_t stream) {
   if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (!configured[device]) {
+    void* ctx = current_context();
+    if (ctx == nullptr || configured[device] != ctx) {
       e = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
-      configured[device] = true;
+      configured[device] = ctx;
     }
   }
   plan_kernel<<<1, kThreads, smem, stream>>>(a);

@@ -54,8 +54,8 @@ class DecodeArgs(ctypes.Structure):
 DTYPE_F16, DTYPE_BF16, DTYPE_E4M3 = 0, 1, 2
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error"}
 EXPORTS = ("sgld_abi_version", "sgld_last_error", "sgld_layer_workspace_bytes", "sgld_plan_build",
-           "sgld_decode_persistent", "sgld_merge_splits")
-ABI_VERSION = 6
+           "sgld_decode_persistent", "sgld_merge_splits", "sgld_decode_persistent_noalloc")
+ABI_VERSION = 7
 
 _lock = threading.Lock()
 _lib = None
@@ -91,6 +91,8 @@ def load(path=None):
         lib.sgld_decode_persistent.restype = ctypes.c_int
         lib.sgld_decode_persistent.argtypes = [ctypes.POINTER(DecodeArgs), ctypes.POINTER(PlanBuffersC),
                                                ctypes.POINTER(PlanGeometry), ctypes.c_void_p]
+        lib.sgld_decode_persistent_noalloc.restype = ctypes.c_int
+        lib.sgld_decode_persistent_noalloc.argtypes = lib.sgld_decode_persistent.argtypes
         lib.sgld_merge_splits.restype = ctypes.c_int
         lib.sgld_merge_splits.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int32] * 5 + [ctypes.c_void_p]
         if lib.sgld_abi_version() != ABI_VERSION:

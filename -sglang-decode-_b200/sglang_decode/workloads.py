@@ -91,7 +91,10 @@ def update_plan(engine, lengths, splits=None):
 
 @dataclass
 class Baseline:
-    """One BASELINE.json configuration (SURVEY section 8(d) recipes)."""
+    """One benchmark configuration (C1..C5): shapes, dtype, KV layout and seeded lengths.
+
+    Inputs follow the reference fixture recipe (``benchmarks/workloads.py:14-40``):
+    N(0,1) values from a seeded generator, splits = ``split_hints(lengths, 16)``."""
     name: str
     config: DecodeConfig
     dtype: torch.dtype

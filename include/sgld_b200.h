@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define SGLD_ABI_VERSION 6
+#define SGLD_ABI_VERSION 7
 
 typedef enum sgld_status {
   SGLD_OK = 0,
@@ -171,17 +171,22 @@ int sgld_merge_splits(const float* partial, const float* lse, const int32_t* cou
                       int32_t query_heads, int32_t head_dim, int32_t max_splits, void* stream);
 
 /*
- * Allocation-free variant of sgld_decode_persistent for callers that cannot allocate
- * device memory (no counterpart in the reference).  Hosts such as plugin interfaces that
- * pass only input and output buffers, or servers that give all device memory to their
- * KV-cache pool at start-up, have no place to put per-layer scratch.  Here the scratch
- * (claim counter, status, fp32 partials and LSEs) lives in a 16 MiB device array owned by
- * the library on every GPU that loads it; args->counter, ->partial and ->lse are ignored,
- * args->status is used when non-NULL.  Geometries needing more than 16 MiB
- * (Bcap*Hq*Smax*(D+1)*4 bytes plus 256) are rejected with SGLD_ERR_INVALID_ARGUMENT.
- * Nothing is allocated.  The first call on a device looks up the array's device address
- * (make it before any stream capture).  All calls share the array: calls whose GPU work
- * overlaps race and must be serialised by the caller.
+ * Allocation-free variant of sgld_decode_persistent (no counterpart in the reference).
+ * For callers that cannot allocate device memory: plugin interfaces that pass only input
+ * and output buffers, or servers that give all device memory to their KV-cache pool at
+ * start-up (cudaMalloc would also synchronise the device inside the serving loop).  The
+ * decode's scratch (claim counter, exit ticket, fp32 partials and LSEs) lives in a 16 MiB
+ * device array owned by the library on every GPU that loads it; args->counter, ->partial
+ * and ->lse are ignored.  args->status must be a caller-owned device word (NULL is
+ * rejected): bounded-wait and slot errors are reported there, as for
+ * sgld_decode_persistent.  A geometry is accepted when
+ *     256 + round_up(Bcap*Hq*Smax*D*4, 256) + round_up(Bcap*Hq*Smax*4, 256) <= 16 MiB
+ * (Bcap = batch_capacity, Hq = query_heads, Smax = max_splits, D = head_dim); larger ones
+ * return SGLD_ERR_INVALID_ARGUMENT.  Every argument is checked before anything is
+ * enqueued.  Nothing is allocated.  The first call on a device (and the first after a
+ * device reset) looks up the array's device address: make it before any stream capture.
+ * All calls share the array: calls whose GPU work overlaps race and must be serialised by
+ * the caller.
  */
 int sgld_decode_persistent_noalloc(const sgld_decode_args* args, const sgld_plan_buffers* plan,
                                    const sgld_plan_geometry* geometry, void* stream);
