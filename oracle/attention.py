@@ -53,6 +53,21 @@ def _attend(qr: np.ndarray, key: np.ndarray, value: np.ndarray, group: int, scal
     return out.reshape(qr.shape)
 
 
+def request_attention(qr, key, value, scale=None, logit_cap=0.0):
+    """One request's FP32 decode (reference/attention.py:10-17 for a single row):
+    qr [Hq, D], key/value [T, Hkv, D] already gathered in token order -> [Hq, D] FP32.
+
+    For callers that gather a request's rows themselves (e.g. on the device, to upcast
+    only those rows): ``paged_attention`` / ``csr_attention`` are this plus the gather."""
+    scale = qr.shape[-1] ** -0.5 if scale is None else scale
+    group = qr.shape[0] // key.shape[1]
+    if group * key.shape[1] != qr.shape[0]:
+        raise ValueError("query heads must be a multiple of KV heads")
+    if key.shape[0] == 0:
+        return np.zeros(qr.shape, dtype=np.float32)
+    return _attend(qr, key, value, group, scale, logit_cap)
+
+
 def paged_attention(q, k, v, pages, lengths, page_size, scale=None, logit_cap=0.0):
     """FP32 paged decode oracle (reference/attention.py:5-18).
 

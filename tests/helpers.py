@@ -90,3 +90,40 @@ def assert_within_tolerance(actual, expected, n, max_abs=2e-2, mean_abs=2e-3):
     worst, mean = A.tolerance_report(got, exp)
     assert worst <= max_abs and mean <= mean_abs, (worst, mean)
     return worst, mean
+
+
+def oracle_requests(q, k, v, lengths, *, indptr=None, indices=None, pages=None, page_size=1,
+                    requests=None, scale=None, logit_cap=0.0):
+    """FP32 oracle rows [len(lengths), Hq, D] for ``requests`` (default: every request).
+
+    Each request's K/V rows are gathered on their own device in token order (CSR:
+    ``indices[indptr[r] + t]``; paged: ``pages[r, t // page_size]``, row ``t % page_size``)
+    and only those rows are upcast and copied to the host, so pools of many GB can be
+    checked.  Rows of requests not selected stay zero."""
+    wanted = range(len(lengths)) if requests is None else requests
+    out = np.zeros((len(lengths), q.shape[1], q.shape[2]), dtype=np.float32)
+    starts = indptr.cpu().tolist() if indptr is not None else None
+    for r in wanted:
+        n = int(lengths[r])
+        if n == 0:
+            continue
+        if starts is not None:
+            rows = indices[starts[r]:starts[r] + n].long()
+            key, value = k[rows], v[rows]
+        else:
+            t = torch.arange(n, device=k.device)
+            phys = pages[r, t // page_size].long()
+            key, value = k[phys, t % page_size], v[phys, t % page_size]
+        out[r] = A.request_attention(f32(q[r]), f32(key), f32(value), scale, logit_cap)
+    return out
+
+
+def assert_rows_within_tolerance(actual, expected, rows, max_abs=2e-2, mean_abs=2e-3):
+    """The tolerance bar on the selected request rows only."""
+    rows = list(rows)
+    got = f32(actual)[rows]
+    exp = np.asarray(expected)[rows]
+    assert np.isfinite(got).all(), "non-finite output"
+    worst, mean = A.tolerance_report(got, exp)
+    assert worst <= max_abs and mean <= mean_abs, (worst, mean)
+    return worst, mean
