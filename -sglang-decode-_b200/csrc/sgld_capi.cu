@@ -97,6 +97,32 @@ bool encode_paged_map(CUtensorMap* map, const void* base, int32_t dtype, int64_t
   return r == CUDA_SUCCESS;
 }
 
+// 3D map {D, Hq, rows} over Q with element strides (head, request); boxes of {64 dims,
+// 16 heads, 1 request} land in shared memory with the 128-byte swizzle.  Heads past Hq and
+// requests past `rows` read as zeros.
+bool encode_q_map(CUtensorMap* map, const void* base, int32_t dtype, int64_t d, int64_t hq, int64_t rows,
+                  const int64_t* stride) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u) != 0 || stride[2] != 1) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(hq), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride[1]) * 2, static_cast<cuuint64_t>(stride[0]) * 2};
+  for (cuuint64_t st : strides)
+    if (st == 0 || st % 16 != 0 || st >= (cuuint64_t{1} << 40)) return false;
+  cuuint32_t box[3] = {64, 16, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType type =
+      dtype == SGLD_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, type, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// SGLD_DECODE_KERNEL=mma keeps every launch on the mma.sync kernel (for A/B measurement).
+bool tc_disabled_by_env() {
+  const char* v = std::getenv("SGLD_DECODE_KERNEL");
+  return v != nullptr && std::strcmp(v, "mma") == 0;
+}
+
 bool tma_disabled_by_env() {
   const char* v = std::getenv("SGLD_DISABLE_TMA");
   return v != nullptr && v[0] == '1';
@@ -240,17 +266,18 @@ void* current_context() {
 
 extern "C" {
 
-int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers* plan,
-                           const sgld_plan_geometry* geometry, void* stream) {
-  int rc = sgld::validate_decode(args, plan, geometry);
-  if (rc) return rc;
-  const sgld_decode_args& d = *args;
+}  // extern "C"
+
+namespace {
+
+// Fill the kernel parameter block of a validated call and choose the kernel; returns an
+// SGLD_KERNEL_* value.
+int prepare_launch(const sgld_decode_args& d, const sgld_plan_buffers* plan, const sgld_plan_geometry* geometry,
+                   sgld::DecodeLaunch& a) {
   const bool kv_fp8 = d.kv_dtype == SGLD_DTYPE_E4M3;
   const int group = d.query_heads / d.kv_heads;
   const bool csr = d.indptr != nullptr;
   const int32_t q_rows = d.q_rows == 0 ? geometry->batch_capacity : d.q_rows;
-  const bool kv_write = d.new_loc != nullptr;
-  sgld::DecodeLaunch a;
   std::memset(&a, 0, sizeof(a));
   a.d = d;
   a.p = *plan;
@@ -271,22 +298,62 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   a.q_rows = q_rows;
   a.fast_kv = fast_kv ? 1 : 0;
   a.fast_q = (aligned16(d.q) && d.q_stride[2] == 1 && d.q_stride[0] % 8 == 0 && d.q_stride[1] % 8 == 0) ? 1 : 0;
-  // Paged KV by tensor-map TMA: a box of 32 tokens never crosses a page because stages
-  // start 32-token aligned and 32 divides the page size.  Smaller pages stay on the
-  // multi-warp cp.async path, which measured faster than 8- or 16-row boxes.  So do
+  const int ps = d.page_size;
+  const bool pageable_tma = !csr && fast_kv && ps % 32 == 0 && d.kv_extent > 0 &&
+                            d.kv_extent < (int64_t{1} << 31) && !tma_disabled_by_env();
+  // The tcgen05 kernel: head_dim 128, 16-bit K/V in 16-byte rows, Q loadable by a TMA box.
+  if (!kv_fp8 && d.head_dim == 128 && fast_kv && a.fast_q && !tc_disabled_by_env() &&
+      encode_q_map(&a.qmap, d.q, d.dtype, d.head_dim, d.query_heads, q_rows, d.q_stride)) {
+    if (pageable_tma &&
+        encode_paged_map(&a.kmap, d.k, d.dtype, d.head_dim, d.kv_heads, ps, d.kv_extent, d.k_stride, 32) &&
+        encode_paged_map(&a.vmap, d.v, d.dtype, d.head_dim, d.kv_heads, ps, d.kv_extent, d.v_stride, 32)) {
+      a.tma_kv = 1;
+      a.box_rows = 32;
+      return SGLD_KERNEL_TCGEN05_TMA;
+    }
+    return SGLD_KERNEL_TCGEN05;
+  }
+  // mma.sync kernel.  Paged KV by tensor-map TMA: a box of 32 tokens never crosses a page
+  // because stages start 32-token aligned and 32 divides the page size.  Smaller pages stay
+  // on the multi-warp cp.async path, which measured faster than 8- or 16-row boxes.  So do
   // D <= 128 kernels with a group of at most 8: they carry 10 cp.async producer warps,
   // which outrun a single thread issuing boxes (C4, page 64: 982 vs 1080 us).
-  const int ps = d.page_size;
   const bool wide_cp_async = d.head_dim <= 128 && group <= 8;
-  if (!csr && !kv_fp8 && fast_kv && ps % 32 == 0 && !wide_cp_async && d.kv_extent > 0 &&
-      d.kv_extent < (int64_t{1} << 31) && !tma_disabled_by_env()) {
+  if (!kv_fp8 && pageable_tma && !wide_cp_async) {
     const int box_rows = 32;
     if (encode_paged_map(&a.kmap, d.k, d.dtype, d.head_dim, d.kv_heads, ps, d.kv_extent, d.k_stride, box_rows) &&
         encode_paged_map(&a.vmap, d.v, d.dtype, d.head_dim, d.kv_heads, ps, d.kv_extent, d.v_stride, box_rows)) {
       a.tma_kv = 1;
       a.box_rows = box_rows;
+      return SGLD_KERNEL_MMA_SYNC_TMA;
     }
   }
+  return SGLD_KERNEL_MMA_SYNC;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sgld_decode_kernel_kind(const sgld_decode_args* args, const sgld_plan_buffers* plan,
+                            const sgld_plan_geometry* geometry) {
+  const int rc = sgld::validate_decode(args, plan, geometry);
+  if (rc) return -rc;
+  sgld::DecodeLaunch a;
+  return prepare_launch(*args, plan, geometry, a);
+}
+
+int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers* plan,
+                           const sgld_plan_geometry* geometry, void* stream) {
+  int rc = sgld::validate_decode(args, plan, geometry);
+  if (rc) return rc;
+  const sgld_decode_args& d = *args;
+  const bool kv_fp8 = d.kv_dtype == SGLD_DTYPE_E4M3;
+  const int32_t q_rows = d.q_rows == 0 ? geometry->batch_capacity : d.q_rows;
+  const bool kv_write = d.new_loc != nullptr;
+  const int ps = d.page_size;
+  sgld::DecodeLaunch a;
+  const int kind = prepare_launch(d, plan, geometry, a);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (kv_write) {   // the step's KV-cache write, chained right before the decode
@@ -312,7 +379,8 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
     e = sgld::launch_kv_write(kw, st, true);
     if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent KV-cache write launch");
   }
-  e = sgld::launch_decode(a, st);
+  e = (kind == SGLD_KERNEL_TCGEN05 || kind == SGLD_KERNEL_TCGEN05_TMA) ? sgld::launch_decode_tc(a, st)
+                                                                        : sgld::launch_decode(a, st);
   if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent launch");
   e = sgld::launch_merge(d.partial, d.lse, plan->counts, plan->error, d.out, d.dtype, geometry->batch_capacity,
                          d.query_heads, d.head_dim, geometry->max_splits, st, true);

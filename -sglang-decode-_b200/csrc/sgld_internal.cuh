@@ -32,6 +32,7 @@ cudaError_t launch_plan(const PlanLaunch& a, cudaStream_t stream);
 struct alignas(64) DecodeLaunch {
   CUtensorMap kmap;  // 4D tensor maps {D, Hkv, page_size, pages} of K and V (paged TMA path)
   CUtensorMap vmap;
+  CUtensorMap qmap;  // 3D tensor map {D, Hq, q_rows} of Q (tcgen05 kernel)
   sgld_decode_args d;
   sgld_plan_buffers p;
   int32_t bcap, smax, workers, group_size;
@@ -67,6 +68,8 @@ struct KVWrite {
 cudaError_t launch_kv_write(const KVWrite& kv, cudaStream_t stream, bool programmatic);
 
 cudaError_t launch_decode(const DecodeLaunch& a, cudaStream_t stream);
+// tcgen05 kernel (head_dim 128, 16-bit K/V, 16-byte aligned rows, qmap encoded).
+cudaError_t launch_decode_tc(const DecodeLaunch& a, cudaStream_t stream);
 
 // Record `msg` as the calling host thread's sgld_last_error() message; returns `code`.
 int set_last_error(int code, const char* msg);

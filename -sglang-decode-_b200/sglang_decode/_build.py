@@ -17,8 +17,8 @@ CSRC = PACKAGE.parent / "csrc"
 INCLUDE = PACKAGE.parent.parent / "include"
 LIB_DIR = PACKAGE / "_lib"
 LIB_NAME = "libsgld_sm100.so"
-SOURCES = ("sgld_plan.cu", "sgld_decode.cu", "sgld_merge.cu", "sgld_kvwrite.cu", "sgld_capi.cu",
-           "sgld_noalloc.cu")
+SOURCES = ("sgld_plan.cu", "sgld_decode.cu", "sgld_decode_tc.cu", "sgld_merge.cu", "sgld_kvwrite.cu",
+           "sgld_capi.cu", "sgld_noalloc.cu")
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 
 

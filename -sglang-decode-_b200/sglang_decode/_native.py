@@ -54,8 +54,10 @@ class DecodeArgs(ctypes.Structure):
 DTYPE_F16, DTYPE_BF16, DTYPE_E4M3 = 0, 1, 2
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error"}
 EXPORTS = ("sgld_abi_version", "sgld_last_error", "sgld_layer_workspace_bytes", "sgld_plan_build",
-           "sgld_decode_persistent", "sgld_merge_splits", "sgld_decode_persistent_noalloc")
-ABI_VERSION = 7
+           "sgld_decode_persistent", "sgld_merge_splits", "sgld_decode_persistent_noalloc",
+           "sgld_decode_kernel_kind")
+ABI_VERSION = 8
+KERNEL_KINDS = {0: "mma.sync", 1: "tcgen05", 2: "tcgen05+tma", 3: "mma.sync+tma"}
 
 _lock = threading.Lock()
 _lib = None
@@ -93,6 +95,8 @@ def load(path=None):
                                                ctypes.POINTER(PlanGeometry), ctypes.c_void_p]
         lib.sgld_decode_persistent_noalloc.restype = ctypes.c_int
         lib.sgld_decode_persistent_noalloc.argtypes = lib.sgld_decode_persistent.argtypes
+        lib.sgld_decode_kernel_kind.restype = ctypes.c_int
+        lib.sgld_decode_kernel_kind.argtypes = lib.sgld_decode_persistent.argtypes[:3]
         lib.sgld_merge_splits.restype = ctypes.c_int
         lib.sgld_merge_splits.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int32] * 5 + [ctypes.c_void_p]
         if lib.sgld_abi_version() != ABI_VERSION:
@@ -126,6 +130,14 @@ def decode_persistent(args_c, plan_c, geometry_c, stream):
     rc = load().sgld_decode_persistent(ctypes.byref(args_c), ctypes.byref(plan_c),
                                        ctypes.byref(geometry_c), stream)
     check(rc, "sgld_decode_persistent")
+
+
+def decode_kernel_kind(args_c, plan_c, geometry_c) -> str:
+    """Name of the decode kernel sgld_decode_persistent launches for these arguments."""
+    rc = load().sgld_decode_kernel_kind(ctypes.byref(args_c), ctypes.byref(plan_c), ctypes.byref(geometry_c))
+    if rc < 0:
+        check(-rc, "sgld_decode_kernel_kind")
+    return KERNEL_KINDS[rc]
 
 
 def merge_splits(partial, lse, counts, error, out, dtype, batch_capacity, query_heads, head_dim,

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define SGLD_ABI_VERSION 7
+#define SGLD_ABI_VERSION 8
 
 typedef enum sgld_status {
   SGLD_OK = 0,
@@ -190,6 +190,24 @@ int sgld_merge_splits(const float* partial, const float* lse, const int32_t* cou
  */
 int sgld_decode_persistent_noalloc(const sgld_decode_args* args, const sgld_plan_buffers* plan,
                                    const sgld_plan_geometry* geometry, void* stream);
+
+/* Decode kernels (see sgld_decode_kernel_kind). */
+enum {
+  SGLD_KERNEL_MMA_SYNC = 0,      /* mma.sync kernel, cp.async or element copies of K/V rows        */
+  SGLD_KERNEL_TCGEN05 = 1,       /* tcgen05.mma kernel, TMEM accumulators, cp.async K/V rows        */
+  SGLD_KERNEL_TCGEN05_TMA = 2,   /* tcgen05.mma kernel, paged K/V by tensor-map TMA boxes           */
+  SGLD_KERNEL_MMA_SYNC_TMA = 3   /* mma.sync kernel, paged K/V by tensor-map TMA boxes              */
+};
+
+/*
+ * Which decode kernel sgld_decode_persistent would launch for these arguments (an
+ * SGLD_KERNEL_* value), or minus an sgld_status when the arguments are invalid.  Nothing is
+ * enqueued.  The tcgen05 kernel serves head_dim 128 with 16-bit K/V in 16-byte aligned rows
+ * and a Q whose rows are 16-byte aligned; other geometries use the mma.sync kernel.  No
+ * counterpart in the reference (its only kernel is the Triton one).
+ */
+int sgld_decode_kernel_kind(const sgld_decode_args* args, const sgld_plan_buffers* plan,
+                            const sgld_plan_geometry* geometry);
 
 /* Bytes of per-layer scratch (counter, partial, lse, status) for one decode
  * layer -- reference runtime/workspace.py:33-40 (LayerBuffers.allocate). */
