@@ -117,10 +117,12 @@ bool encode_q_map(CUtensorMap* map, const void* base, int32_t dtype, int64_t d, 
   return r == CUDA_SUCCESS;
 }
 
-// SGLD_DECODE_KERNEL=mma keeps every launch on the mma.sync kernel (for A/B measurement).
-bool tc_disabled_by_env() {
+// Kernel choice.  SGLD_DECODE_KERNEL=tcgen05 selects the tcgen05 kernel wherever it applies,
+// =mma the mma.sync kernel everywhere; unset, the measured-faster kernel for the geometry is
+// used (currently the mma.sync kernel: see the decode kernels' design notes).
+bool use_tc_kernel() {
   const char* v = std::getenv("SGLD_DECODE_KERNEL");
-  return v != nullptr && std::strcmp(v, "mma") == 0;
+  return v != nullptr && std::strcmp(v, "tcgen05") == 0;
 }
 
 bool tma_disabled_by_env() {
@@ -302,7 +304,7 @@ int prepare_launch(const sgld_decode_args& d, const sgld_plan_buffers* plan, con
   const bool pageable_tma = !csr && fast_kv && ps % 32 == 0 && d.kv_extent > 0 &&
                             d.kv_extent < (int64_t{1} << 31) && !tma_disabled_by_env();
   // The tcgen05 kernel: head_dim 128, 16-bit K/V in 16-byte rows, Q loadable by a TMA box.
-  if (!kv_fp8 && d.head_dim == 128 && fast_kv && a.fast_q && !tc_disabled_by_env() &&
+  if (!kv_fp8 && d.head_dim == 128 && fast_kv && a.fast_q && use_tc_kernel() &&
       encode_q_map(&a.qmap, d.q, d.dtype, d.head_dim, d.query_heads, q_rows, d.q_stride)) {
     if (pageable_tma &&
         encode_paged_map(&a.kmap, d.k, d.dtype, d.head_dim, d.kv_heads, ps, d.kv_extent, d.k_stride, 32) &&

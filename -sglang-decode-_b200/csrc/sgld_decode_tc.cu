@@ -82,41 +82,44 @@ constexpr int kHalf = kTS * 128;               // bytes of one 64-dim half of a 
 constexpr int kQRows = 16;                     // MMA N: query heads of a group, padded
 constexpr int kQBytes = kQRows * kD * 2;       // 4 KB
 constexpr int kPBytes = kTS * kQRows * 2;      // 4 KB
+constexpr int kPBufs = 4;                      // P buffers: the softmax runs up to 3 tiles ahead of PV
 constexpr int kSD = 4;                         // stage-descriptor ring depth
 constexpr int kNB = 2;                         // stages indexed per round trip
-constexpr int kSDEntry = kTS * 24;             // koff, voff (int64), page, row (int32)
+constexpr int kSDEntry = kTS * 8;              // page (or CSR slot) and row in page, int32 each
 constexpr int kTaskQ = 4;
 constexpr int kHdrQ = 4;                       // softmax header ring
-constexpr int kSoftmaxWarps = 4;
-constexpr int kMmaWarp = 4;
-constexpr int kProducerWarp0 = 5;
-constexpr int kProducerWarps = 8;
+constexpr int kSoftmaxWarps = 8;               // two groups of four: each group owns half the head columns
+constexpr int kMmaWarp = kSoftmaxWarps;
+constexpr int kProducerWarp0 = kMmaWarp + 1;
+constexpr int kProducerWarps = 8;              // copy_tile covers 16 rows per step with 8 warps
 constexpr int kIndexerWarp = kProducerWarp0 + kProducerWarps;
 constexpr int kSchedulerWarp = kIndexerWarp + 1;
 constexpr int kWarps = kSchedulerWarp + 1;
 constexpr int kThreads = kWarps * 32;
-constexpr int kTmemCols = 64;                  // S[2] (16 columns each), O[2] (16 each)
+constexpr int kSBufs = 4;                      // TMEM score buffers (QK runs up to 3 tiles ahead)
+constexpr int kTmemCols = 128;                 // S[4] (16 columns each), O[2] (16 each) at column 64
 constexpr int kOffQ = kStages * kStage;
 constexpr int kOffP = kOffQ + 2 * kQBytes;
-constexpr int kOffSD = kOffP + 2 * kPBytes;
+constexpr int kOffSD = kOffP + kPBufs * kPBytes;
 constexpr int kOffMisc = kOffSD + kSD * kSDEntry;
-constexpr int kMiscBytes = 2048;
+constexpr int kMiscBytes = 3072;
 constexpr int kSmemUsed = kOffMisc + kMiscBytes;
 constexpr int kSmemBytes = kSmemUsed + 1024;   // launch size including 1 KB alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 
 struct Misc {
   uint64_t full_k[kStages], full_v[kStages], empty_k[kStages], empty_v[kStages];
-  uint64_t s_full[2], s_free[2], p_full[2], p_free[2];
+  uint64_t s_full[kSBufs], s_free[kSBufs], p_full[kPBufs], p_free[kPBufs];
   uint64_t q_full[2], q_empty[2], o_full[2], o_free[2];
   uint64_t tfull[kTaskQ], tempty[kTaskQ], sdfull[kSD], sdempty[kSD], hfull[kHdrQ], hempty[kHdrQ];
-  uint64_t join[2], join_l[2], drain;
+  uint64_t join[2][2], join_l[2][2], drain;   // [column group][parity]
   Hdr hdr[kStages];       // data ring headers (MMA issuer)
+  int4 pend[kSBufs];      // MMA issuer: (stage, phase, task, flags) of tiles awaiting PV
   Hdr shdr[kSD];          // descriptor ring headers (producers)
   Hdr xhdr[kHdrQ];        // softmax header ring
   Task tq[kTaskQ];
-  alignas(16) float red[2][kSoftmaxWarps][16];     // per-warp tile maxima (read as float4)
-  alignas(16) float red_l[2][kSoftmaxWarps][16];   // per-warp row sums at a task's end
+  alignas(16) float red[2][4][16];     // [tile parity][TMEM quadrant][head]: per-warp tile maxima
+  alignas(16) float red_l[2][4][16];   // [task parity][quadrant][head]: per-warp row sums at a task's end
   uint32_t tmem_base;
 };
 static_assert(sizeof(Misc) <= kMiscBytes, "misc area too small");
@@ -128,27 +131,97 @@ __device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
   return static_cast<uint32_t>(((chunk >> 3) * ROWS + row) * 128 + (((chunk & 7) ^ (row & 7)) << 4));
 }
 
+// Bounded waits.  The common case (phase already complete, or completing within try_wait's
+// own suspend window) stays inline; the deadline loop is out of line to keep every call site
+// small (instruction-cache misses are a measured stall of this kernel).
+//
+// Waiting warps issue instructions while they poll, and most of this kernel's warps wait most
+// of the time, so roles off the critical path (scheduler, indexer, producers) sleep between
+// polls (kBackoffNs); the softmax warps and the MMA issuer poll promptly.
+constexpr uint32_t kBackoffNs = 128;
+
+__device__ __noinline__ bool wait_slow(uint64_t* bar, uint32_t parity) {
+  return mbar_wait(bar, parity, global_timer_ns() + kWaitLimitNs);
+}
+
+__device__ __noinline__ bool wait_slow_backoff(uint64_t* bar, uint32_t parity) {
+  const uint64_t deadline = global_timer_ns() + kWaitLimitNs;
+  while (!mbar_try_wait(bar, parity)) {
+    __nanosleep(kBackoffNs);
+    if (global_timer_ns() > deadline) return false;
+  }
+  return true;
+}
+
+template <bool kBackoff = false>
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* status, int code) {
-  const bool ok = mbar_wait(bar, parity, global_timer_ns() + kWaitLimitNs);
+  const bool ok = mbar_try_wait(bar, parity) || (kBackoff ? wait_slow_backoff(bar, parity) : wait_slow(bar, parity));
   if (!ok) atomicOr(status, code);
   return ok;
 }
 
 // Bounded wait that also reconverges the warp.
+template <bool kBackoff = false>
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
-  const bool ok = mbar_wait(bar, parity, global_timer_ns() + kWaitLimitNs);
+  const bool ok = mbar_try_wait(bar, parity) || (kBackoff ? wait_slow_backoff(bar, parity) : wait_slow(bar, parity));
   __syncwarp();
   if (!ok && (threadIdx.x & 31) == 0) atomicOr(status, code);
   return ok;
 }
 
-// NH: query-head columns the softmax handles (8 for groups <= 8, else 16); the MMAs always
-// use N = 16 and P columns past NH are zero.
-template <typename T, int NH>
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld<2>(uint32_t taddr, float (&v)[2]) {
+  uint32_t r0, r1;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  v[0] = __uint_as_float(r0), v[1] = __uint_as_float(r1);
+}
+template <>
+__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, float (&v)[4]) {
+  uint32_t r[4];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, float (&v)[8]) {
+  tmem_ld8(taddr, v);
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const float (&v)[N]);
+template <>
+__device__ __forceinline__ void tmem_st<2>(uint32_t taddr, const float (&v)[2]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1,%2};" ::"r"(taddr), "r"(__float_as_uint(v[0])),
+               "r"(__float_as_uint(v[1])) : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st<4>(uint32_t taddr, const float (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(__float_as_uint(v[0])),
+               "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])) : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st<8>(uint32_t taddr, const float (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])) : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// NHW: head columns per softmax warp (two groups cover 2*NHW heads: 4, 8 or 16 for groups of up
+// to 4, 8 or 16).  The MMAs always use N = 16; P columns past 2*NHW stay zero.
+template <typename T, int NHW>
 struct TcKernel {
   // ------------------------------------------------------------------ scheduler (lane 0)
   __device__ static bool push_task(Misc& ms, int& ti, uint32_t& tph, const Task& t, int* status) {
-    if (!wait_bar(&ms.tempty[ti], tph ^ 1u, status, kStatusWaitTask)) return false;
+    if (!wait_bar<true>(&ms.tempty[ti], tph ^ 1u, status, kStatusWaitTask)) return false;
     ms.tq[ti] = t;
     mbar_arrive(&ms.tfull[ti]);
     if (++ti == kTaskQ) {
@@ -283,7 +356,7 @@ struct TcKernel {
       nxt.tb = cur.tb + kNB * kTS;
       return true;
     }
-    if (!warp_wait(&ms.tfull[ti], tph, status, kStatusWaitTask)) return false;
+    if (!warp_wait<true>(&ms.tfull[ti], tph, status, kStatusWaitTask)) return false;
     nxt.t = ms.tq[ti];
     __syncwarp();
     if (lane == 0) mbar_arrive(&ms.tempty[ti]);
@@ -298,8 +371,6 @@ struct TcKernel {
   __device__ static void indexer(const DecodeLaunch& a, unsigned char* smem, Misc& ms) {
     const int lane = threadIdx.x & 31;
     int* status = a.d.status;
-    const int64_t* ks = a.d.k_stride;
-    const int64_t* vs = a.d.v_stride;
     int ti = 0, sd = 0;
     uint32_t tph = 0, sph = 0;
     Batch b, n;
@@ -313,19 +384,13 @@ struct TcKernel {
       for (int i = 0; i < kNB; ++i) {
         const int t0 = b.tb + i * kTS;
         if (t0 >= b.t.end) break;
-        ok = warp_wait(&ms.sdempty[sd], sph ^ 1u, status, kStatusWaitDesc);
+        ok = warp_wait<true>(&ms.sdempty[sd], sph ^ 1u, status, kStatusWaitDesc);
         if (!ok) break;
-        unsigned char* entry = smem + kOffSD + sd * kSDEntry;
-        int64_t* koff = reinterpret_cast<int64_t*>(entry);
-        int64_t* voff = koff + kTS;
-        int* page = reinterpret_cast<int*>(voff + kTS);
+        int* page = reinterpret_cast<int*>(smem + kOffSD + sd * kSDEntry);
         int* row = page + kTS;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int64_t pr = b.phys[i][u], in = b.inner[i][u];
           const int j = u * 32 + lane;
-          koff[j] = pr * ks[0] + in * ks[1] + static_cast<int64_t>(b.t.group) * ks[2];
-          voff[j] = pr * vs[0] + in * vs[1] + static_cast<int64_t>(b.t.group) * vs[2];
           page[j] = b.phys[i][u];
           row[j] = b.inner[i][u];
         }
@@ -365,13 +430,22 @@ struct TcKernel {
   // ------------------------------------------------------------------ producers
   // 16-byte cp.async of one 128-token tile; rows at or past ntok are zero-filled (the PV
   // MMA multiplies them by P = 0, so they must hold finite values).
-  __device__ static void copy_tile(uint32_t dst, const T* base, const int64_t* off, int ntok, int pw, int lane) {
-#pragma unroll 4
-    for (int i = pw * 32 + lane; i < kTS * 16; i += kProducerWarps * 32) {
-      const int jt = i >> 4, c = i & 15;
+  // Thread (pw, lane) copies chunk c = lane % 16 of rows jt0 + 16k (jt0 = 2 pw + lane / 16):
+  // rows 16 apart share the swizzle phase, so their offsets step by 16 rows of 128 bytes.
+  // Row jt lives at page[jt] * st[0] + row[jt] * st[1] + group * st[2] elements (CSR: st[1] = 0).
+  __device__ static void copy_tile(uint32_t dst, const T* base, const int* page, const int* row, const int64_t* st,
+                                   int group, int ntok, int pw, int lane) {
+    static_assert(kProducerWarps * 2 == 16, "eight producer warps cover 16 rows per step");
+    const int c = lane & 15, jt0 = pw * 2 + (lane >> 4);
+    const uint32_t d0 = dst + tile_off<kTS>(jt0, c);
+    const T* base_c = base + static_cast<int64_t>(group) * st[2] + c * 8;
+    const int64_t s0 = st[0], s1 = st[1];
+#pragma unroll
+    for (int k = 0; k < kTS / 16; ++k) {
+      const int jt = jt0 + 16 * k;
       const bool live = jt < ntok;
-      const T* src = live ? base + off[jt] + c * 8 : base;
-      cp_async_16_fill(dst + tile_off<kTS>(jt, c), src, live ? 16u : 0u);
+      const T* src = live ? base_c + page[jt] * s0 + row[jt] * s1 : base;
+      cp_async_16_fill(d0 + k * 16 * 128, src, live ? 16u : 0u);
     }
   }
 
@@ -387,18 +461,15 @@ struct TcKernel {
     uint32_t sph = 0, ph = 0, hph = 0;
     bool ok = true;
     while (true) {
-      ok = warp_wait(&ms.sdfull[sd], sph, status, kStatusWaitDesc);
+      ok = warp_wait<true>(&ms.sdfull[sd], sph, status, kStatusWaitDesc);
       if (!ok) break;
       const Hdr h = ms.shdr[sd];
       if (h.flags & kFlagExit) break;
-      const unsigned char* entry = smem + kOffSD + sd * kSDEntry;
-      const int64_t* koff = reinterpret_cast<const int64_t*>(entry);
-      const int64_t* voff = koff + kTS;
-      const int* page = reinterpret_cast<const int*>(voff + kTS);
+      const int* page = reinterpret_cast<const int*>(smem + kOffSD + sd * kSDEntry);
       const int* prow = page + kTS;
       if ((h.flags & kFlagFirst) && pw == 0) {
         const int qb = qcount & 1;
-        ok = warp_wait(&ms.q_empty[qb], ((qcount >> 1) & 1) ^ 1u, status, kStatusWaitQ);
+        ok = warp_wait<true>(&ms.q_empty[qb], ((qcount >> 1) & 1) ^ 1u, status, kStatusWaitQ);
         if (!ok) break;
         if (lane == 0) {
           // A request past q's rows reads zeros: the box is out of bounds of the tensor map.
@@ -415,7 +486,7 @@ struct TcKernel {
       const uint32_t vdst = kdst + kTile;
       const int nchunks = (h.ntok + 31) >> 5;   // TMA boxes of 32 tokens
       // ---- K tile
-      ok = warp_wait(&ms.empty_k[s], ph ^ 1u, status, kStatusWaitEmpty);
+      ok = warp_wait<true>(&ms.empty_k[s], ph ^ 1u, status, kStatusWaitEmpty);
       if (!ok) break;
       if (a.tma_kv) {
         if (lane == 0) {
@@ -430,7 +501,7 @@ struct TcKernel {
         __syncwarp();
         mbar_arrive(&ms.full_k[s]);
       } else {
-        copy_tile(kdst, kbase, koff, h.ntok, pw, lane);
+        copy_tile(kdst, kbase, page, prow, a.d.k_stride, h.group, h.ntok, pw, lane);
         cp_async_arrive_noinc(&ms.full_k[s]);
         if (lead) {
           ms.hdr[s] = h;
@@ -438,7 +509,7 @@ struct TcKernel {
         }
       }
       // ---- V tile
-      ok = warp_wait(&ms.empty_v[s], ph ^ 1u, status, kStatusWaitEmpty);
+      ok = warp_wait<true>(&ms.empty_v[s], ph ^ 1u, status, kStatusWaitEmpty);
       if (!ok) break;
       if (a.tma_kv) {
         if (lane == 0) {
@@ -452,13 +523,13 @@ struct TcKernel {
         __syncwarp();
         mbar_arrive(&ms.full_v[s]);
       } else {
-        copy_tile(vdst, vbase, voff, h.ntok, pw, lane);
+        copy_tile(vdst, vbase, page, prow, a.d.v_stride, h.group, h.ntok, pw, lane);
         cp_async_arrive_noinc(&ms.full_v[s]);
         if (lead) mbar_arrive(&ms.full_v[s]);
       }
       // ---- the softmax warps' copy of the header
       if (pw == 0) {
-        ok = warp_wait(&ms.hempty[hs], hph ^ 1u, status, kStatusWaitEmpty);
+        ok = warp_wait<true>(&ms.hempty[hs], hph ^ 1u, status, kStatusWaitEmpty);
         if (!ok) break;
         if (lane == 0) {
           ms.xhdr[hs] = h;
@@ -504,104 +575,115 @@ struct TcKernel {
   }
 
   // ------------------------------------------------------------------ MMA issuer (lane 0)
-  struct Pending {
-    int s, tile, task, flags;
-    uint32_t ph;
-  };
-
-  __device__ static bool issue_pv(const DecodeLaunch& a, unsigned char* smem, Misc& ms, uint32_t tmem,
-                                  const Pending& u, bool tma_kv) {
-    int* status = a.d.status;
-    if (!wait_bar(&ms.full_v[u.s], u.ph, status, kStatusWaitFull)) return false;
-    if (!wait_bar(&ms.p_full[u.tile & 1], (u.tile >> 1) & 1, status, kStatusWaitFull)) return false;
-    const int ob = u.task & 1;
-    const bool first = (u.flags & kFlagFirst) != 0;
-    if (first && !wait_bar(&ms.o_free[ob], ((u.task >> 1) & 1) ^ 1u, status, kStatusWaitFull)) return false;
-    if (!tma_kv) fence_proxy_async_smem();   // cp.async rows landed through the generic proxy
-    tc_fence_after();
-    constexpr uint32_t idesc = mma_idesc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u, 1u, 1u, 16u, 128u);
-    const uint32_t vb = smem_addr(smem + u.s * kStage + kTile);
-    const uint32_t pb = smem_addr(smem + kOffP + (u.tile & 1) * kPBytes);
-    const uint32_t d = tmem + 32 + ob * 16;
-#pragma unroll
-    for (int ks = 0; ks < kTS / 16; ++ks)
-      mma_f16(d, smem_desc(vb + ks * 2048, kHalf, 1024, 2), smem_desc(pb + ks * 512, 256, 128, 0), idesc,
-              (first && ks == 0) ? 0u : 1u);
-    mma_commit(&ms.empty_v[u.s]);
-    mma_commit(&ms.p_free[u.tile & 1]);
-    if (u.flags & kFlagLast) mma_commit(&ms.o_full[ob]);
-    return true;
-  }
-
+  // An event loop over two in-order streams of work: QK of the next tile (its K tile has
+  // landed, a score buffer is free; up to kSBufs tiles ahead of the softmax) and PV of the
+  // oldest tile whose P is ready.  Neither waits for the other, so the tensor cores' latency
+  // overlaps the softmax instead of adding to it.
   __device__ static void mma_issuer(const DecodeLaunch& a, unsigned char* smem, Misc& ms, uint32_t tmem) {
     int* status = a.d.status;
-    constexpr uint32_t idesc = mma_idesc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u, 0u, 0u, 16u, 128u);
-    int s = 0, tile = 0, qtask = 0;
-    uint32_t ph = 0;
-    bool pending = false, ok = true;
-    Pending prev{};
-    while (ok) {
-      if (!wait_bar(&ms.full_k[s], ph, status, kStatusWaitFull)) {
-        ok = false;
-        break;
-      }
-      const Hdr h = ms.hdr[s];
-      if (h.flags & kFlagExit) break;
-      const bool first = (h.flags & kFlagFirst) != 0;
-      if (first) ++qtask;
-      const int task = qtask - 1, qb = task & 1;
-      if (first && !wait_bar(&ms.q_full[qb], (task >> 1) & 1, status, kStatusWaitQ)) {
-        ok = false;
-        break;
-      }
-      if (!wait_bar(&ms.s_free[tile & 1], ((tile >> 1) & 1) ^ 1u, status, kStatusWaitFull)) {
-        ok = false;
-        break;
-      }
-      if (!a.tma_kv) fence_proxy_async_smem();
-      tc_fence_after();
-      const uint32_t kb = smem_addr(smem + s * kStage);
-      const uint32_t qbase = smem_addr(smem + kOffQ + qb * kQBytes);
-      const uint32_t d = tmem + (tile & 1) * 16;
+    constexpr uint32_t bf = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+    constexpr uint32_t idesc_qk = mma_idesc(bf, 0u, 0u, 16u, 128u);
+    constexpr uint32_t idesc_pv = mma_idesc(bf, 1u, 1u, 16u, 128u);
+    int sq = 0, tq = 0, tp = 0, qtask = 0;
+    uint32_t phq = 0;
+    bool exit_seen = false;
+    uint64_t deadline = global_timer_ns() + kWaitLimitNs;
+    int idle = 0;
+    while (!(exit_seen && tp == tq)) {
+      bool progressed = false;
+      // ---- QK of tile tq
+      if (!exit_seen && tq - tp < kSBufs && mbar_test_wait(&ms.full_k[sq], phq)) {
+        const Hdr h = ms.hdr[sq];
+        if (h.flags & kFlagExit) {
+          exit_seen = true;
+          progressed = true;
+        } else {
+          const bool first = (h.flags & kFlagFirst) != 0;
+          const int task = first ? qtask : qtask - 1, qb = task & 1;
+          if ((!first || mbar_test_wait(&ms.q_full[qb], (task >> 1) & 1)) &&
+              mbar_test_wait(&ms.s_free[tq & (kSBufs - 1)], ((tq / kSBufs) & 1) ^ 1u)) {
+            if (first) ++qtask;
+            if (!a.tma_kv) fence_proxy_async_smem();   // cp.async rows arrived through the generic proxy
+            tc_fence_after();
+            const uint32_t kb = smem_addr(smem + sq * kStage);
+            const uint32_t qbase = smem_addr(smem + kOffQ + qb * kQBytes);
+            const uint32_t d = tmem + (tq & (kSBufs - 1)) * 16;
 #pragma unroll
-      for (int ks = 0; ks < kD / 16; ++ks)
-        mma_f16(d, smem_desc(kb + (ks >> 2) * kHalf + (ks & 3) * 32, 16, 1024, 2),
-                smem_desc(qbase + (ks >> 2) * (kQRows * 128) + (ks & 3) * 32, 16, 1024, 2), idesc, ks > 0 ? 1u : 0u);
-      mma_commit(&ms.s_full[tile & 1]);
-      mma_commit(&ms.empty_k[s]);
-      if (h.flags & kFlagLast) mma_commit(&ms.q_empty[qb]);
-      // PV one tile behind: the softmax of this tile overlaps the previous tile's PV.
-      if (pending && !issue_pv(a, smem, ms, tmem, prev, a.tma_kv)) {
-        ok = false;
-        pending = false;
-        break;
+            for (int ks = 0; ks < kD / 16; ++ks)
+              mma_f16(d, smem_desc(kb + (ks >> 2) * kHalf + (ks & 3) * 32, 16, 1024, 2),
+                      smem_desc(qbase + (ks >> 2) * (kQRows * 128) + (ks & 3) * 32, 16, 1024, 2), idesc_qk,
+                      ks > 0 ? 1u : 0u);
+            mma_commit(&ms.s_full[tq & (kSBufs - 1)]);
+            mma_commit(&ms.empty_k[sq]);
+            if (h.flags & kFlagLast) mma_commit(&ms.q_empty[qb]);
+            ms.pend[tq & (kSBufs - 1)] = make_int4(sq, static_cast<int>(phq), task, h.flags);
+            ++tq;
+            if (++sq == kStages) {
+              sq = 0;
+              phq ^= 1u;
+            }
+            progressed = true;
+          }
+        }
       }
-      prev = Pending{s, tile, task, h.flags, ph};
-      pending = true;
-      ++tile;
-      if (++s == kStages) {
-        s = 0;
-        ph ^= 1u;
+      // ---- PV of tile tp
+      if (tp < tq) {
+        const int4 u = ms.pend[tp & (kSBufs - 1)];   // stage, phase, task, flags
+        const bool first = (u.w & kFlagFirst) != 0;
+        const int ob = u.z & 1;
+        if (mbar_test_wait(&ms.p_full[tp % kPBufs], (tp / kPBufs) & 1) && mbar_test_wait(&ms.full_v[u.x], u.y) &&
+            (!first || mbar_test_wait(&ms.o_free[ob], ((u.z >> 1) & 1) ^ 1u))) {
+          if (!a.tma_kv) fence_proxy_async_smem();
+          tc_fence_after();
+          const uint32_t vb = smem_addr(smem + u.x * kStage + kTile);
+          const uint32_t pb = smem_addr(smem + kOffP + (tp % kPBufs) * kPBytes);
+          const uint32_t d = tmem + 64 + ob * 16;
+#pragma unroll
+          for (int ks = 0; ks < kTS / 16; ++ks)
+            mma_f16(d, smem_desc(vb + ks * 2048, kHalf, 1024, 2), smem_desc(pb + ks * 512, 256, 128, 0), idesc_pv,
+                    (first && ks == 0) ? 0u : 1u);
+          mma_commit(&ms.empty_v[u.x]);
+          mma_commit(&ms.p_free[tp % kPBufs]);
+          if (u.w & kFlagLast) mma_commit(&ms.o_full[ob]);
+          ++tp;
+          progressed = true;
+        }
+      }
+      if (progressed) {
+        idle = 0;
+      } else {
+        __nanosleep(32);   // leave the issue slots to the softmax warp on this sub-partition
+        if ((++idle & 63) == 0) {
+          if (idle == 64) deadline = global_timer_ns() + kWaitLimitNs;
+          else if (global_timer_ns() > deadline) {
+            atomicOr(status, kStatusWaitFull);
+            break;
+          }
+        }
       }
     }
-    if (ok && pending) issue_pv(a, smem, ms, tmem, prev, a.tma_kv);
     // Wait until every MMA this thread issued has completed (tensor memory is released after).
     mma_commit(&ms.drain);
     wait_bar(&ms.drain, 0, status, kStatusWaitFull);
   }
 
-  // ------------------------------------------------------------------ softmax (4 warps)
-  // Max over the warp of x[i] (i < NH) per column i; lanes 2i and 2i+1 end with column i's
-  // result (transposed butterfly: each exchange halves the columns a lane keeps).
+  // ------------------------------------------------------------------ softmax (8 warps)
+  // Warp w covers TMEM quadrant q = w % 4 (lanes 32q..32q+31: tokens of the scores, dims of
+  // the output) and head columns [g*NHW, g*NHW + NHW) with g = w / 4.  The two column groups
+  // share the tile stream and nothing else: each keeps its own joins, reference maxima, row
+  // sums, rescaling and epilogue.
+
+  // Reduction over the warp of x[i] per column i (max or sum); afterwards lane l holds column
+  // reduced_col(l) (transposed butterfly: each exchange halves the columns a lane keeps).
   template <bool kSum>
-  __device__ static float warp_reduce_cols(const float (&x)[NH]) {
+  __device__ static float warp_reduce_cols(const float (&x)[NHW]) {
     const int lane = threadIdx.x & 31;
-    float v[NH];
+    float v[NHW];
 #pragma unroll
-    for (int i = 0; i < NH; ++i) v[i] = x[i];
+    for (int i = 0; i < NHW; ++i) v[i] = x[i];
     auto op = [](float p, float q) { return kSum ? p + q : fmaxf(p, q); };
 #pragma unroll
-    for (int width = NH / 2, bit = 16; width >= 1; width >>= 1, bit >>= 1) {
+    for (int width = NHW / 2, bit = 16; width >= 1; width >>= 1, bit >>= 1) {
       const bool upper = (lane & bit) != 0;
 #pragma unroll
       for (int i = 0; i < width; ++i) {
@@ -610,32 +692,69 @@ struct TcKernel {
         v[i] = op(keep, __shfl_xor_sync(0xffffffffu, send, bit));
       }
     }
-    // NH = 16: four exchanges leave one column per lane pair (bits 4..1); NH = 8: three leave
-    // one column per lane quad (bits 4..2).  Finish over the remaining lane bits.
+    // log2(NHW) exchanges used lane bits 16 .. 32/NHW; finish over the lower bits.
     float r = v[0];
 #pragma unroll
-    for (int bit = (NH == 16 ? 1 : 2); bit >= 1; bit >>= 1) r = op(r, __shfl_xor_sync(0xffffffffu, r, bit));
+    for (int bit = 16 / NHW; bit >= 1; bit >>= 1) r = op(r, __shfl_xor_sync(0xffffffffu, r, bit));
     return r;
   }
 
-  // Column owned by this lane after warp_reduce_cols.
-  __device__ static int reduced_col(int lane) { return NH == 16 ? (lane >> 1) : (lane >> 2); }
+  __device__ static int reduced_col(int lane) { return lane / (32 / NHW); }
+  __device__ static bool col_writer(int lane) { return (lane % (32 / NHW)) == 0; }
+
+  // Task end: normalise this warp's columns of O^T and store partial rows and LSE.
+  __device__ static bool epilogue(const DecodeLaunch& a, Misc& ms, uint32_t tmem, const Hdr& h, int task,
+                                  const float (&m)[NHW], const float (&lsum)[NHW]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, q = warp & 3, g = warp >> 2;
+    int* status = a.d.status;
+    const int ob = task & 1;
+    if (!warp_wait(&ms.o_full[ob], (task >> 1) & 1, status, kStatusWaitFull)) return false;
+    tc_fence_after();
+    float o[NHW];
+    tmem_ld<NHW>(tmem + (static_cast<uint32_t>(q * 32) << 16) + 64 + ob * 16 + g * NHW, o);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ms.o_free[ob]);
+    const float wl = warp_reduce_cols<true>(lsum);
+    if (col_writer(lane)) ms.red_l[ob][q][g * NHW + reduced_col(lane)] = wl;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ms.join_l[g][ob]);
+    if (!warp_wait(&ms.join_l[g][ob], (task >> 1) & 1, status, kStatusWaitFull)) return false;
+    const int gs = a.group_size, smax = a.smax;
+    const int64_t slot0 = (static_cast<int64_t>(h.request) * a.d.query_heads + h.group * gs) * smax + h.split;
+#pragma unroll
+    for (int i = 0; i < NHW; ++i) {
+      const int head = g * NHW + i;
+      if (head < gs) {
+        const float l = ms.red_l[ob][0][head] + ms.red_l[ob][1][head] + ms.red_l[ob][2][head] + ms.red_l[ob][3][head];
+        const int64_t slot = slot0 + static_cast<int64_t>(head) * smax;
+        a.d.partial[slot * kD + q * 32 + lane] = o[i] * __fdividef(a.d.v_scale, l);
+        if (q == 0 && lane == i) a.d.lse[slot] = (m[i] + lg2(l)) * kLn2;
+      }
+    }
+    return true;
+  }
 
   __device__ static void softmax(const DecodeLaunch& a, unsigned char* smem, Misc& ms, uint32_t tmem) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, q = warp & 3, g = warp >> 2;
     int* status = a.d.status;
     const float cap = a.d.logit_cap;
     const bool capped = cap > 0.f;
     const float sc = (capped ? a.d.scale : a.d.scale * kLog2e) * a.d.k_scale;
     const float cap_log2e = cap * kLog2e, two_log2e_over_cap = capped ? 2.f * kLog2e / cap : 0.f;
-    const int hq = a.d.query_heads, gs = a.group_size, smax = a.smax;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const int tok = warp * 32 + lane;
-    float m_ref[NH], lsum[NH];
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const int tok = q * 32 + lane, col0 = g * NHW;
+    float m_ref[NHW], lsum[NHW];
 #pragma unroll
-    for (int i = 0; i < NH; ++i) m_ref[i] = 0.f, lsum[i] = 0.f;
+    for (int i = 0; i < NHW; ++i) m_ref[i] = 0.f, lsum[i] = 0.f;
+    // The previous task's epilogue runs after the next tile's P is published, so the wait
+    // for its last PV overlaps that tile.
+    bool pending = false;
+    Hdr ph{};
+    int ptask = 0;
+    float pm[NHW], pl[NHW];
     int tile = 0, task = 0, hs = 0, s = 0;
-    uint32_t hph = 0, ph = 0;
+    uint32_t hph = 0, ph_v = 0;
     while (true) {
       if (!warp_wait(&ms.hfull[hs], hph, status, kStatusWaitFull)) return;
       const Hdr h = ms.xhdr[hs];
@@ -647,137 +766,113 @@ struct TcKernel {
       }
       if (h.flags & kFlagExit) break;
       const bool first = (h.flags & kFlagFirst) != 0;
-      // ---- scores of this warp's 32 tokens
-      if (!warp_wait(&ms.s_full[tile & 1], (tile >> 1) & 1, status, kStatusWaitFull)) return;
+      // ---- scores of this warp's 32 tokens and NHW heads
+      const int sb = tile & (kSBufs - 1);
+      if (!warp_wait(&ms.s_full[sb], (tile / kSBufs) & 1, status, kStatusWaitFull)) return;
       tc_fence_after();
-      float x[NH];
-      {
-        float sv[16];
-        tmem_ld16(tmem + lane_base + (tile & 1) * 16, sv);
-#pragma unroll
-        for (int i = 0; i < NH; ++i) x[i] = sv[i];
-      }
+      float x[NHW];
+      tmem_ld<NHW>(tmem + lane_base + sb * 16 + col0, x);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ms.s_free[tile & 1]);
+      if (lane == 0) mbar_arrive(&ms.s_free[sb]);
       const bool valid = tok < h.ntok;
 #pragma unroll
-      for (int i = 0; i < NH; ++i) {
+      for (int i = 0; i < NHW; ++i) {
         float y = x[i] * sc;
         if (capped) y = cap_log2e * (1.f - 2.f / (ex2(y * two_log2e_over_cap) + 1.f));
         x[i] = valid ? y : -INFINITY;
       }
-      // ---- tile maximum per head over the 128 tokens
+      // ---- tile maximum per head over the 128 tokens (four quadrants of this group)
       const float wmax = warp_reduce_cols<false>(x);
-      const int col = reduced_col(lane);
       const int jb = tile & 1;
-      if ((lane & (NH == 16 ? 1 : 3)) == 0) ms.red[jb][warp][col] = wmax;
+      if (col_writer(lane)) ms.red[jb][q][col0 + reduced_col(lane)] = wmax;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ms.join[jb]);
-      if (!warp_wait(&ms.join[jb], (tile >> 1) & 1, status, kStatusWaitFull)) return;
-      float tmax[NH];
+      if (lane == 0) mbar_arrive(&ms.join[g][jb]);
+      if (!warp_wait(&ms.join[g][jb], (tile >> 1) & 1, status, kStatusWaitFull)) return;
+      float tmax[NHW];
 #pragma unroll
-      for (int i = 0; i < NH; i += 4) {
-        float4 r = *reinterpret_cast<const float4*>(&ms.red[jb][0][i]);
-#pragma unroll
-        for (int w = 1; w < kSoftmaxWarps; ++w) {
-          const float4 q = *reinterpret_cast<const float4*>(&ms.red[jb][w][i]);
-          r.x = fmaxf(r.x, q.x), r.y = fmaxf(r.y, q.y), r.z = fmaxf(r.z, q.z), r.w = fmaxf(r.w, q.w);
-        }
-        tmax[i] = r.x, tmax[i + 1] = r.y, tmax[i + 2] = r.z, tmax[i + 3] = r.w;
-      }
+      for (int i = 0; i < NHW; ++i)
+        tmax[i] = fmaxf(fmaxf(ms.red[jb][0][col0 + i], ms.red[jb][1][col0 + i]),
+                        fmaxf(ms.red[jb][2][col0 + i], ms.red[jb][3][col0 + i]));
       if (first) {
 #pragma unroll
-        for (int i = 0; i < NH; ++i) m_ref[i] = tmax[i], lsum[i] = 0.f;
+        for (int i = 0; i < NHW; ++i) m_ref[i] = tmax[i], lsum[i] = 0.f;
       } else {
         bool grow = false;
 #pragma unroll
-        for (int i = 0; i < NH; ++i) grow |= tmax[i] > m_ref[i] + kRescaleLog2;
-        if (grow) {   // uniform over the four warps (same maxima): rescale O in tensor memory
-          if (!warp_wait(&ms.p_free[(tile - 1) & 1], ((tile - 1) >> 1) & 1, status, kStatusWaitFull)) return;
+        for (int i = 0; i < NHW; ++i) grow |= tmax[i] > m_ref[i] + kRescaleLog2;
+        if (grow) {   // uniform over the group (same maxima): rescale its O columns in TMEM
+          if (!warp_wait(&ms.p_free[(tile - 1) % kPBufs], ((tile - 1) / kPBufs) & 1, status, kStatusWaitFull)) return;
           tc_fence_after();
-          float o[16];
-          const uint32_t taddr = tmem + lane_base + 32 + (task & 1) * 16;
-          tmem_ld16(taddr, o);
+          float o[NHW];
+          const uint32_t taddr = tmem + lane_base + 64 + (task & 1) * 16 + col0;
+          tmem_ld<NHW>(taddr, o);
 #pragma unroll
-          for (int i = 0; i < NH; ++i) {
+          for (int i = 0; i < NHW; ++i) {
             const float mn = fmaxf(m_ref[i], tmax[i]);
             const float alpha = ex2(m_ref[i] - mn);
             o[i] *= alpha;
             lsum[i] *= alpha;
             m_ref[i] = mn;
           }
-          tmem_st16(taddr, o);
+          tmem_st<NHW>(taddr, o);
         }
       }
-      // ---- P = 2^(x - m) as the B operand of the PV MMA (MN-major, no swizzle: 8x8 core
-      //      matrices, token blocks 256 bytes apart, head blocks 128 bytes apart)
-      if (!warp_wait(&ms.p_free[tile & 1], ((tile >> 1) & 1) ^ 1u, status, kStatusWaitFull)) return;
-      uint32_t pk[8];
+      // ---- P = 2^(x - m): this group's heads of the token's 16-head row of the B operand
+      //      (MN-major, no swizzle: token blocks of 8 are 256 bytes apart, heads 8-15 at +128)
+      if (!warp_wait(&ms.p_free[tile % kPBufs], ((tile / kPBufs) & 1) ^ 1u, status, kStatusWaitFull)) return;
+      uint32_t pk[NHW / 2];
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        float p0 = 0.f, p1 = 0.f;
-        if (i < NH) {
-          p0 = valid ? ex2(x[i] - m_ref[i]) : 0.f;
-          p1 = valid ? ex2(x[i + 1] - m_ref[i + 1]) : 0.f;
-          lsum[i] += p0;
-          lsum[i + 1] += p1;
-        }
+      for (int i = 0; i < NHW; i += 2) {
+        const float p0 = valid ? ex2(x[i] - m_ref[i]) : 0.f;
+        const float p1 = valid ? ex2(x[i + 1] - m_ref[i + 1]) : 0.f;
+        lsum[i] += p0;
+        lsum[i + 1] += p1;
         pk[i / 2] = Mma<T>::pack(p0, p1);
       }
-      unsigned char* pbuf = smem + kOffP + (tile & 1) * kPBytes + (tok >> 3) * 256 + (tok & 7) * 16;
-      *reinterpret_cast<uint4*>(pbuf) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      *reinterpret_cast<uint4*>(pbuf + 128) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      unsigned char* prow = smem + kOffP + (tile % kPBufs) * kPBytes + (tok >> 3) * 256 + (tok & 7) * 16 +
+                            (col0 >> 3) * 128 + (col0 & 7) * 2;
+      if constexpr (NHW == 8) {
+        *reinterpret_cast<uint4*>(prow) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      } else if constexpr (NHW == 4) {
+        *reinterpret_cast<uint2*>(prow) = make_uint2(pk[0], pk[1]);
+      } else {
+        *reinterpret_cast<uint32_t*>(prow) = pk[0];
+      }
       // Rows of V past the tile's last token must be finite (P = 0 multiplies them): the
-      // cp.async path zero-fills them; with tensor-map boxes this thread clears its row.
+      // cp.async path zero-fills them; with tensor-map boxes the two groups clear the row.
       if (a.tma_kv && h.ntok < kTS) {
-        if (!warp_wait(&ms.full_v[s], ph, status, kStatusWaitFull)) return;
+        if (!warp_wait(&ms.full_v[s], ph_v, status, kStatusWaitFull)) return;
         if (!valid) {
-          unsigned char* vrow = smem + s * kStage + kTile;
+          unsigned char* vt = smem + s * kStage + kTile;
 #pragma unroll
-          for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4*>(vrow + tile_off<kTS>(tok, c)) = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(vt + tile_off<kTS>(tok, g * 8 + c)) = make_uint4(0, 0, 0, 0);
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ms.p_full[tile & 1]);
-      // ---- task end: normalise and store the partial output and LSE of every head
+      if (lane == 0) mbar_arrive(&ms.p_full[tile % kPBufs]);
+      if (pending) {
+        if (!epilogue(a, ms, tmem, ph, ptask, pm, pl)) return;
+        pending = false;
+      }
       if (h.flags & kFlagLast) {
-        const int ob = task & 1;
-        if (!warp_wait(&ms.o_full[ob], (task >> 1) & 1, status, kStatusWaitFull)) return;
-        tc_fence_after();
-        float o[16];
-        tmem_ld16(tmem + lane_base + 32 + ob * 16, o);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ms.o_free[ob]);
-        const float wl = warp_reduce_cols<true>(lsum);
-        if ((lane & (NH == 16 ? 1 : 3)) == 0) ms.red_l[ob][warp][col] = wl;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ms.join_l[ob]);
-        if (!warp_wait(&ms.join_l[ob], (task >> 1) & 1, status, kStatusWaitFull)) return;
-        const int64_t slot0 = (static_cast<int64_t>(h.request) * hq + h.group * gs) * smax + h.split;
-        const float vs = a.d.v_scale;
+        pending = true;
+        ph = h;
+        ptask = task;
 #pragma unroll
-        for (int i = 0; i < NH; ++i) {
-          if (i < gs) {
-            float l = ms.red_l[ob][0][i];
-#pragma unroll
-            for (int w = 1; w < kSoftmaxWarps; ++w) l += ms.red_l[ob][w][i];
-            const int64_t slot = slot0 + static_cast<int64_t>(i) * smax;
-            a.d.partial[slot * kD + tok] = o[i] / l * vs;   // tok doubles as the dim index here
-            if (warp == 0 && lane == i) a.d.lse[slot] = (m_ref[i] + lg2(l)) * kLn2;
-          }
-        }
+        for (int i = 0; i < NHW; ++i) pm[i] = m_ref[i], pl[i] = lsum[i];
         ++task;
       }
       ++tile;
       if (++s == kStages) {
         s = 0;
-        ph ^= 1u;
+        ph_v ^= 1u;
       }
     }
+    if (pending) epilogue(a, ms, tmem, ph, ptask, pm, pl);
   }
 
   // ------------------------------------------------------------------ entry
@@ -794,17 +889,23 @@ struct TcKernel {
         mbar_init(&ms.empty_k[i], 1);
         mbar_init(&ms.empty_v[i], 1);
       }
-      for (int i = 0; i < 2; ++i) {
+      for (int i = 0; i < kSBufs; ++i) {
         mbar_init(&ms.s_full[i], 1);
         mbar_init(&ms.s_free[i], kSoftmaxWarps);
+      }
+      for (int i = 0; i < kPBufs; ++i) {
         mbar_init(&ms.p_full[i], kSoftmaxWarps);
         mbar_init(&ms.p_free[i], 1);
+      }
+      for (int i = 0; i < 2; ++i) {
         mbar_init(&ms.q_full[i], 1);
         mbar_init(&ms.q_empty[i], 1);
         mbar_init(&ms.o_full[i], 1);
         mbar_init(&ms.o_free[i], kSoftmaxWarps);
-        mbar_init(&ms.join[i], kSoftmaxWarps);
-        mbar_init(&ms.join_l[i], kSoftmaxWarps);
+        for (int g = 0; g < 2; ++g) {
+          mbar_init(&ms.join[g][i], kSoftmaxWarps / 2);
+          mbar_init(&ms.join_l[g][i], kSoftmaxWarps / 2);
+        }
       }
       for (int i = 0; i < kTaskQ; ++i) {
         mbar_init(&ms.tfull[i], 1);
@@ -821,6 +922,10 @@ struct TcKernel {
       mbar_init(&ms.drain, 1);
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    // P columns past the heads the softmax writes stay zero for the whole launch.
+    for (int i = threadIdx.x; i < kPBufs * kPBytes / 16; i += kThreads)
+      reinterpret_cast<uint4*>(smem + kOffP)[i] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
     if (warp == kMmaWarp) tmem_alloc(smem_addr(&ms.tmem_base), kTmemCols);
     tc_fence_before();
     __syncthreads();
@@ -858,12 +963,12 @@ struct TcKernel {
   }
 };
 
-template <typename T, int NH>
+template <typename T, int NHW>
 __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_constant__ DecodeLaunch a) {
-  TcKernel<T, NH>::run(a);
+  TcKernel<T, NHW>::run(a);
 }
 
-template <typename T, int NH>
+template <typename T, int NHW>
 cudaError_t launch_tc_typed(const DecodeLaunch& a, cudaStream_t stream) {
   constexpr int kMaxDevices = 64;
   static std::atomic<void*> configured[kMaxDevices] = {};   // context the attribute was set in
@@ -873,7 +978,7 @@ cudaError_t launch_tc_typed(const DecodeLaunch& a, cudaStream_t stream) {
   if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
   void* ctx = current_context();
   if (ctx == nullptr || configured[device].load(std::memory_order_acquire) != ctx) {
-    e = cudaFuncSetAttribute(decode_tc_kernel<T, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    e = cudaFuncSetAttribute(decode_tc_kernel<T, NHW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
     configured[device].store(ctx, std::memory_order_release);
   }
@@ -887,16 +992,19 @@ cudaError_t launch_tc_typed(const DecodeLaunch& a, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_tc_kernel<T, NH>, a);
+  return cudaLaunchKernelEx(&cfg, decode_tc_kernel<T, NHW>, a);
 }
 
 }  // namespace
 
 cudaError_t launch_decode_tc(const DecodeLaunch& a, cudaStream_t stream) {
-  const bool wide = a.group_size > 8;
-  if (a.d.dtype == SGLD_DTYPE_BF16)
-    return wide ? launch_tc_typed<__nv_bfloat16, 16>(a, stream) : launch_tc_typed<__nv_bfloat16, 8>(a, stream);
-  return wide ? launch_tc_typed<__half, 16>(a, stream) : launch_tc_typed<__half, 8>(a, stream);
+  const int g = a.group_size;   // head columns per softmax warp: half the padded group
+  if (a.d.dtype == SGLD_DTYPE_BF16) {
+    if (g <= 4) return launch_tc_typed<__nv_bfloat16, 2>(a, stream);
+    return g <= 8 ? launch_tc_typed<__nv_bfloat16, 4>(a, stream) : launch_tc_typed<__nv_bfloat16, 8>(a, stream);
+  }
+  if (g <= 4) return launch_tc_typed<__half, 2>(a, stream);
+  return g <= 8 ? launch_tc_typed<__half, 4>(a, stream) : launch_tc_typed<__half, 8>(a, stream);
 }
 
 }  // namespace sgld

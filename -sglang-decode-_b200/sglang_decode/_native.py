@@ -61,6 +61,7 @@ KERNEL_KINDS = {0: "mma.sync", 1: "tcgen05", 2: "tcgen05+tma", 3: "mma.sync+tma"
 
 _lock = threading.Lock()
 _lib = None
+_ops = None
 
 
 class NativeError(RuntimeError):
@@ -104,6 +105,25 @@ def load(path=None):
         if path is None:
             _lib = lib
         return lib
+
+
+def ops():
+    """The torch operator library (``torch.ops.sglang_decode``: plan_build, decode, merge),
+    loaded once; it calls the C ABI of ``libsgld_sm100.so``.  Raises if it is not built."""
+    global _ops
+    if _ops is not None:
+        return _ops
+    load()                                         # the C ABI library first (version check; takes _lock)
+    with _lock:
+        if _ops is None:
+            import torch
+            path = _build.ops_library_path()
+            if not path.exists():
+                raise RuntimeError(f"{path} is missing: build the extension first (python -m sglang_decode._build "
+                                   "or __graft_entry__.build()); there is no fallback implementation")
+            torch.ops.load_library(str(path))
+            _ops = torch.ops.sglang_decode
+    return _ops
 
 
 def check(rc: int, what: str) -> None:

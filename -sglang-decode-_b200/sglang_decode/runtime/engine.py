@@ -6,9 +6,10 @@ Same API and checks as the reference's ``runtime/engine.py:1-74``:
 ``execute(q, k, v, pages, layer=0, *, indptr=None, scale=None, logit_cap=0.0)`` (paged
 ``[page, token, head, dim]`` or CSR ``[token, head, dim]`` KV, arbitrary strides).
 ``execute`` enqueues the sm_100a persistent decode kernel and the split merge (a
-programmatic dependent launch that overlaps the decode's tail); the claim counter is
-reset by the plan build and left at zero by the decode launch itself (the
-reference's per-layer memset is not needed).
+programmatic dependent launch that overlaps the decode's tail) through the torch operator
+``torch.ops.sglang_decode.decode``, which calls the C ABI; the claim counter is reset by
+the plan build and left at zero by the decode launch itself (the reference's per-layer
+memset is not needed).
 """
 from dataclasses import dataclass
 
@@ -44,6 +45,7 @@ class DecodeEngine:
         self.plan.register_counters(self.counters)
         self.layers = [LayerBuffers.allocate(config, self.plan.device, dtype, counter=self.counters[i])
                        for i in range(layers)]
+        self._calls = {}       # layer -> arguments of its last execute (for c_args)
 
     def prepare(self):
         """Call once per compatible group per step, including on every graph replay."""
@@ -87,7 +89,6 @@ class DecodeEngine:
                 raise ValueError("all tensors must live on the engine's device")
         if pages.dtype != torch.int32:
             raise ValueError("page table / kv_indices must be int32")
-        a = out.c_args
         if indptr is None:
             if k.ndim != 4 or v.ndim != 4 or k.shape != v.shape:
                 raise ValueError("paged KV must have matching [page,token,head,dim] shapes")
@@ -95,11 +96,7 @@ class DecodeEngine:
                 raise ValueError("KV geometry differs from the capture configuration")
             if tuple(pages.shape) != (c.batch_capacity, c.max_pages):
                 raise ValueError("page table capacity mismatch")
-            a.k_stride[:] = k.stride()
-            a.v_stride[:] = v.stride()
-            a.pt_stride[:] = pages.stride()
-            a.indptr = None
-            a.page_size = c.page_size
+            page_size = c.page_size
         else:
             if k.ndim != 3 or v.shape != k.shape or tuple(k.shape[1:]) != (c.kv_heads, c.head_dim):
                 raise ValueError("CSR KV must be [token,head,dim]")
@@ -107,34 +104,18 @@ class DecodeEngine:
                 raise ValueError("CSR integration uses one-token physical pages")
             if indptr.dtype != torch.int32 or indptr.ndim != 1:
                 raise ValueError("kv_indptr must be a 1-D int32 tensor")
-            ks, vs = k.stride(), v.stride()
-            a.k_stride[:] = (ks[0], 0, ks[1], ks[2])
-            a.v_stride[:] = (vs[0], 0, vs[1], vs[2])
-            a.pt_stride[:] = (0, 0)
-            a.indptr = indptr.data_ptr()
-            a.page_size = 1
-        a.q, a.k, a.v, a.out, a.pages = (q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                         out.output.data_ptr(), pages.data_ptr())
-        a.kv_extent = k.shape[0] if k.shape[0] == v.shape[0] else 0
-        a.q_stride[:] = q.stride()
-        a.dtype = _DTYPES[q.dtype]
-        a.kv_dtype = _native.DTYPE_E4M3 if kv_fp8 else a.dtype
+            page_size = 1
+        k_scale, v_scale = float(k_scale), float(v_scale)
         for name, value in (("k_scale", k_scale), ("v_scale", v_scale)):
-            value = float(value)
             if not value > 0.0 or value == float("inf"):
                 raise ValueError(f"{name} must be a finite value > 0")
-            setattr(a, name, value)
-        a.query_heads, a.kv_heads, a.head_dim = c.query_heads, c.kv_heads, c.head_dim
-        a.scale = c.head_dim ** -0.5 if scale is None else float(scale)
+        scale = c.head_dim ** -0.5 if scale is None else float(scale)
         cap = float(logit_cap or 0.0)
         if not cap >= 0.0 or cap == float("inf"):
             raise ValueError("logit_cap must be a finite value >= 0 (0 disables it)")
-        a.logit_cap = cap
-        a.q_rows = q.shape[0]
         if new_loc is None:
             if k_new is not None or v_new is not None:
                 raise ValueError("k_new / v_new need new_loc")
-            a.k_new = a.v_new = a.new_loc = None
         else:
             rows = q.shape[0]
             for t in (k_new, v_new):
@@ -144,16 +125,49 @@ class DecodeEngine:
             if (new_loc.dtype not in (torch.int64, torch.int32) or new_loc.device != p.device
                     or new_loc.ndim != 1 or new_loc.shape[0] != rows or new_loc.stride(0) != 1):
                 raise ValueError("new_loc must be a contiguous 1-D int64/int32 tensor, one slot per Q row")
-            a.k_new, a.v_new = k_new.data_ptr(), v_new.data_ptr()
+        call = (q, k, v, pages, indptr, out.output, out.partial, out.lse, out.counter, out.status, p.tensors,
+                p.geometry, c.query_heads, c.kv_heads, c.head_dim, page_size, scale, cap, k_scale, v_scale,
+                k_new, v_new, new_loc)
+        self._calls[layer] = call
+        _native.ops().decode(*call)          # torch.ops.sglang_decode.decode -> sgld_decode_persistent
+        return out.output
+
+    def c_args(self, layer=0):
+        """The ``sgld_decode_args`` (ctypes) of this layer's last ``execute`` call, for callers
+        that use the C ABI directly (e.g. ``sgld_decode_kernel_kind`` or the allocation-free
+        entry point).  The struct points at the same tensors as that call."""
+        (q, k, v, pages, indptr, output, partial, lse, counter, status, _, _, hq, hkv, d, page_size, scale, cap,
+         k_scale, v_scale, k_new, v_new, new_loc) = self._calls[layer]
+        a = _native.DecodeArgs()
+        a.q, a.k, a.v, a.out, a.pages = q.data_ptr(), k.data_ptr(), v.data_ptr(), output.data_ptr(), pages.data_ptr()
+        if indptr is None:
+            a.k_stride[:], a.v_stride[:], a.pt_stride[:] = k.stride(), v.stride(), pages.stride()
+            a.indptr = None
+        else:
+            ks, vs = k.stride(), v.stride()
+            a.k_stride[:] = (ks[0], 0, ks[1], ks[2])
+            a.v_stride[:] = (vs[0], 0, vs[1], vs[2])
+            a.pt_stride[:] = (0, 0)
+            a.indptr = indptr.data_ptr()
+        a.page_size = page_size
+        a.kv_extent = k.shape[0] if k.shape[0] == v.shape[0] else 0
+        a.q_stride[:] = q.stride()
+        a.dtype = _DTYPES[q.dtype]
+        a.kv_dtype = _native.DTYPE_E4M3 if k.dtype == _FP8 else a.dtype
+        a.query_heads, a.kv_heads, a.head_dim = hq, hkv, d
+        a.scale, a.logit_cap, a.k_scale, a.v_scale = scale, cap, k_scale, v_scale
+        a.q_rows = q.shape[0]
+        if new_loc is not None:
+            a.k_new, a.v_new, a.new_loc = k_new.data_ptr(), v_new.data_ptr(), new_loc.data_ptr()
             a.knew_stride[:] = k_new.stride()
             a.vnew_stride[:] = v_new.stride()
-            a.new_loc = new_loc.data_ptr()
             a.new_loc_int32 = 1 if new_loc.dtype == torch.int32 else 0
-        a.counter, a.partial, a.lse = out.counter.data_ptr(), out.partial.data_ptr(), out.lse.data_ptr()
-        a.status = out.status.data_ptr()
-        stream = torch.cuda.current_stream(p.device).cuda_stream
-        _native.decode_persistent(a, p.c_buffers, p.c_geometry, stream)
-        return out.output
+        a.counter, a.partial, a.lse, a.status = counter.data_ptr(), partial.data_ptr(), lse.data_ptr(), status.data_ptr()
+        return a
+
+    def kernel_kind(self, layer=0):
+        """Name of the decode kernel this layer's last ``execute`` launched ("tcgen05", ...)."""
+        return _native.decode_kernel_kind(self.c_args(layer), self.plan.c_buffers, self.plan.c_geometry)
 
 
 def merge_splits(partial, lse, counts, error, out):
@@ -165,7 +179,5 @@ def merge_splits(partial, lse, counts, error, out):
     b, hq, smax, d = partial.shape
     if tuple(lse.shape) != (b, hq, smax) or tuple(out.shape) != (b, hq, d) or counts.numel() < b:
         raise ValueError("merge shapes disagree")
-    stream = torch.cuda.current_stream(partial.device).cuda_stream
-    _native.merge_splits(partial.data_ptr(), lse.data_ptr(), counts.data_ptr(), error.data_ptr(),
-                         out.data_ptr(), _DTYPES[out.dtype], b, hq, d, smax, stream)
+    _native.ops().merge(partial, lse, counts, error, out)
     return out

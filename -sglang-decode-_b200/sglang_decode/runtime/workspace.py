@@ -6,7 +6,7 @@ claim counter, fp32 partial/LSE split slots and the output.  Additions of the B2
 kernel: ``LayerBuffers.status`` (bounded-wait error word); ``counter`` has two words
 (claim counter + exit ticket).
 """
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 
@@ -39,6 +39,11 @@ class PlanBuffers:
         self.rule_count = len(rows)
         self.has_static_rule = any(row[4] == 2 for row in rows)
         self.counters = None
+        # Operator views (torch.ops.sglang_decode): the buffers in sgld_plan_buffers order and
+        # the geometry (batch_capacity, max_splits, max_context, groups, workers).
+        self.tensors = [getattr(self, name) for name in _native.PLAN_FIELDS]
+        self.geometry = [config.batch_capacity, config.max_splits, config.max_context, config.kv_heads,
+                         config.workers]
         # C views: pointers are stable for the lifetime of this object.
         self.c_buffers = _native.PlanBuffersC(
             **{name: getattr(self, name).data_ptr() for name in _native.PLAN_FIELDS})
@@ -71,7 +76,6 @@ class LayerBuffers:
     lse: torch.Tensor
     output: torch.Tensor
     status: torch.Tensor = None
-    c_args: object = field(default=None, repr=False)
 
     @classmethod
     def allocate(cls, config, device, dtype=torch.bfloat16, counter=None):
@@ -83,5 +87,4 @@ class LayerBuffers:
                    torch.empty(shape, dtype=torch.float32, device=device),
                    torch.empty((config.batch_capacity, config.query_heads, config.head_dim),
                                dtype=dtype, device=device),
-                   torch.zeros(1, dtype=torch.int32, device=device),
-                   _native.DecodeArgs())
+                   torch.zeros(1, dtype=torch.int32, device=device))

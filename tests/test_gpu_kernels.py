@@ -1,0 +1,128 @@
+"""Both decode kernels against the FP32 oracle: the mma.sync kernel and the tcgen05 kernel
+(QK and PV on tcgen05.mma with tensor-memory accumulators, head_dim 128, 16-bit K/V).
+
+SGLD_DECODE_KERNEL selects the kernel per call ("mma" / "tcgen05"); each case asserts which
+kernel actually ran (sgld_decode_kernel_kind), so a silent fallback cannot pass for coverage.
+Tolerance: max-abs 2e-2, mean-abs 2e-3 against FP32; every dispatch mode bit-identical.
+"""
+import pytest
+import torch
+
+from sglang_decode.config import DecodeConfig, Mode
+from sglang_decode.runtime.engine import DecodeEngine
+from sglang_decode.workloads import baseline, generate, make_csr_inputs, make_inputs, subset, update_plan
+from tests.helpers import assert_rows_within_tolerance, assert_within_tolerance, oracle_csr, oracle_paged, oracle_requests
+
+pytestmark = pytest.mark.gpu
+
+KERNELS = {"mma": {"mma.sync", "mma.sync+tma"}, "tcgen05": {"tcgen05", "tcgen05+tma"}}
+
+
+@pytest.fixture(params=sorted(KERNELS))
+def kernel(request, monkeypatch):
+    monkeypatch.setenv("SGLD_DECODE_KERNEL", request.param)
+    return request.param
+
+
+def _run(engine, inputs, lengths, indptr=None, **kw):
+    update_plan(engine, lengths)
+    engine.layers[0].partial.fill_(float("nan"))
+    engine.prepare()
+    q, k, v, pages = inputs
+    out = engine.execute(q, k, v, pages, indptr=indptr, **kw)
+    torch.cuda.synchronize()
+    assert engine.layers[0].status.item() == 0, "bounded in-kernel wait expired"
+    assert engine.counters.eq(0).all()
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("group", [1, 3, 4, 7, 8, 12, 16])
+def test_csr_groups(kernel, dtype, group):
+    hkv = 2 if group > 4 else 4
+    lengths = [1, 65, 300, 0, 1000, 129, 64, 128]
+    c = DecodeConfig(batch_capacity=8, max_splits=8, max_context=1024, query_heads=hkv * group, kv_heads=hkv,
+                     head_dim=128, page_size=1, workers=37)
+    q, k, v, idx, indptr = (t.cuda() for t in make_csr_inputs(c, lengths, device="cpu", dtype=dtype, pool=4000))
+    expected = oracle_csr(q, k, v, indptr, idx, lengths)
+    outs = []
+    for mode in Mode:
+        engine = DecodeEngine(c, dtype=dtype, force_mode=mode)
+        out = _run(engine, (q, k, v, idx), lengths, indptr=indptr)
+        assert engine.kernel_kind() in KERNELS[kernel]
+        assert_within_tolerance(out, expected, len(lengths))
+        outs.append(out.clone())
+    assert all(torch.equal(outs[0], o) for o in outs[1:]), "every mode gives the same bits"
+
+
+@pytest.mark.parametrize("page_size", [1, 16, 32, 64])
+def test_paged_page_sizes(kernel, page_size):
+    lengths = [700, 3, 64, 129, 2000, 32]
+    c = DecodeConfig(batch_capacity=6, max_splits=4, max_context=2048, query_heads=16, kv_heads=2, head_dim=128,
+                     page_size=page_size, workers=148)
+    inputs = tuple(t.cuda() for t in make_inputs(c, lengths, device="cpu"))
+    engine = DecodeEngine(c, force_mode=Mode.D4)
+    out = _run(engine, inputs, lengths)
+    assert engine.kernel_kind() in KERNELS[kernel]
+    assert_within_tolerance(out, oracle_paged(*inputs, lengths, page_size), len(lengths))
+
+
+@pytest.mark.parametrize("cap", [0.0, 5.0, 30.0])
+def test_logit_cap_and_large_scores(kernel, cap):
+    """Q scaled up so scores reach tens of units: the running maximum grows across tiles, which
+    exercises the tcgen05 kernel's in-place rescale of the output in tensor memory."""
+    lengths = [1000, 300, 900]
+    c = DecodeConfig(batch_capacity=3, max_splits=2, max_context=1024, query_heads=16, kv_heads=2, head_dim=128,
+                     page_size=1, workers=20)
+    q, k, v, idx, indptr = (t.cuda() for t in make_csr_inputs(c, lengths, device="cpu", pool=3000))
+    # Later tokens of each request get larger keys, so tile maxima keep rising.
+    position = torch.zeros(k.shape[0], device="cuda")
+    position[idx.long()] = torch.arange(idx.numel(), device="cuda", dtype=position.dtype) / idx.numel()
+    k = (k.float() * (0.2 + 2.8 * position).view(-1, 1, 1)).to(torch.bfloat16)
+    q = (4.0 * q.float()).to(torch.bfloat16)
+    expected = oracle_csr(q, k, v, indptr, idx, lengths, logit_cap=cap)
+    engine = DecodeEngine(c, force_mode=Mode.R1)
+    out = _run(engine, (q, k, v, idx), lengths, indptr=indptr, logit_cap=cap)
+    assert engine.kernel_kind() in KERNELS[kernel]
+    assert_within_tolerance(out, expected, len(lengths))
+
+
+def test_strided_q_falls_back_to_the_mma_kernel(monkeypatch):
+    """A Q whose rows are not 16-byte aligned cannot be loaded by a TMA box: the call still
+    succeeds on the mma.sync kernel even when tcgen05 is requested."""
+    monkeypatch.setenv("SGLD_DECODE_KERNEL", "tcgen05")
+    lengths = [100, 300]
+    c = DecodeConfig(batch_capacity=2, max_splits=2, max_context=512, query_heads=8, kv_heads=2, head_dim=128,
+                     page_size=1, workers=8)
+    q, k, v, idx, indptr = (t.cuda() for t in make_csr_inputs(c, lengths, device="cpu", pool=512))
+    storage = torch.zeros(2, 8, 129, dtype=q.dtype, device="cuda")
+    storage[..., :128] = q
+    q_odd = storage[..., :128]
+    engine = DecodeEngine(c)
+    out = _run(engine, (q_odd, k, v, idx), lengths, indptr=indptr)
+    assert engine.kernel_kind() == "mma.sync"
+    assert_within_tolerance(out, oracle_csr(q, k, v, indptr, idx, lengths), len(lengths))
+
+
+@pytest.mark.parametrize("name", ["C1", "C2", "C3", "C4"])
+def test_baseline_shapes_on_the_tcgen05_kernel(monkeypatch, name):
+    """The benchmark configurations' real shapes (C3: 16-request prefix, C4: 3 requests)."""
+    monkeypatch.setenv("SGLD_DECODE_KERNEL", "tcgen05")
+    b = baseline(name, workers=torch.cuda.get_device_properties(0).multi_processor_count)
+    b = {"C3": subset(b, 16), "C4": subset(b, 3)}.get(name, b)
+    data = generate(b, device="cuda", seed=17)
+    c = b.config
+    expected = oracle_requests(data["q"], data["k"], data["v"], b.lengths, indptr=data["indptr"],
+                               indices=data["pages"], pages=data["pages"], page_size=c.page_size)
+    outs = []
+    for mode in ((Mode.R1, Mode.D1) if name != "C2" else (Mode.R1, Mode.STATIC, Mode.D1, Mode.D4)):
+        engine = DecodeEngine(c, device="cuda", dtype=b.dtype, force_mode=mode)
+        update_plan(engine, b.lengths, b.splits)
+        engine.prepare()
+        out = engine.execute(data["q"], data["k"], data["v"], data["pages"], indptr=data["indptr"])
+        torch.cuda.synchronize()
+        assert engine.layers[0].status.item() == 0
+        assert engine.kernel_kind() in KERNELS["tcgen05"]
+        assert_rows_within_tolerance(out, expected, range(len(b.lengths)))
+        outs.append(out.clone())
+    assert all(torch.equal(outs[0], o) for o in outs[1:])

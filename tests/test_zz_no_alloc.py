@@ -43,8 +43,7 @@ def _config():
 def _noalloc_call(fn, engine, out, status, **override):
     """Call the entry point with the engine's last sgld_decode_persistent arguments, the
     scratch pointers cleared (the library supplies them) and the given fields replaced."""
-    args = _native.DecodeArgs()
-    ctypes.memmove(ctypes.byref(args), ctypes.byref(engine.layers[0].c_args), ctypes.sizeof(args))
+    args = engine.c_args(0)
     args.out = out.data_ptr()
     args.counter = args.partial = args.lse = None
     args.status = status.data_ptr() if status is not None else None
