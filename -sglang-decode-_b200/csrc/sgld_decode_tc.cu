@@ -702,8 +702,9 @@ struct TcKernel {
   __device__ static int reduced_col(int lane) { return lane / (32 / NHW); }
   __device__ static bool col_writer(int lane) { return (lane % (32 / NHW)) == 0; }
 
-  // Task end: normalise this warp's columns of O^T and store partial rows and LSE.
-  __device__ static bool epilogue(const DecodeLaunch& a, Misc& ms, uint32_t tmem, const Hdr& h, int task,
+  // Task end: normalise this warp's columns of O^T and store partial rows and LSE.  Out of
+  // line: it runs once per task, and the kernel's instruction footprint is a measured stall.
+  __device__ __noinline__ static bool epilogue(const DecodeLaunch& a, Misc& ms, uint32_t tmem, const Hdr& h, int task,
                                   const float (&m)[NHW], const float (&lsum)[NHW]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, q = warp & 3, g = warp >> 2;
     int* status = a.d.status;
@@ -732,6 +733,28 @@ struct TcKernel {
         if (q == 0 && lane == i) a.d.lse[slot] = (m[i] + lg2(l)) * kLn2;
       }
     }
+    return true;
+  }
+
+  // The running maximum of some head grew by more than 2^kRescaleLog2: once the previous
+  // tile's PV has completed, scale this warp's lanes of the group's O columns (and the row
+  // sums) to the new maxima.  Rare; out of line.
+  __device__ __noinline__ static bool rescale(const DecodeLaunch& a, Misc& ms, uint32_t taddr, int tile,
+                                              const float (&tmax)[NHW], float (&m_ref)[NHW], float (&lsum)[NHW]) {
+    if (!warp_wait(&ms.p_free[(tile - 1) % kPBufs], ((tile - 1) / kPBufs) & 1, a.d.status, kStatusWaitFull))
+      return false;
+    tc_fence_after();
+    float o[NHW];
+    tmem_ld<NHW>(taddr, o);
+#pragma unroll
+    for (int i = 0; i < NHW; ++i) {
+      const float mn = fmaxf(m_ref[i], tmax[i]);
+      const float alpha = ex2(m_ref[i] - mn);
+      o[i] *= alpha;
+      lsum[i] *= alpha;
+      m_ref[i] = mn;
+    }
+    tmem_st<NHW>(taddr, o);
     return true;
   }
 
@@ -802,20 +825,7 @@ struct TcKernel {
 #pragma unroll
         for (int i = 0; i < NHW; ++i) grow |= tmax[i] > m_ref[i] + kRescaleLog2;
         if (grow) {   // uniform over the group (same maxima): rescale its O columns in TMEM
-          if (!warp_wait(&ms.p_free[(tile - 1) % kPBufs], ((tile - 1) / kPBufs) & 1, status, kStatusWaitFull)) return;
-          tc_fence_after();
-          float o[NHW];
-          const uint32_t taddr = tmem + lane_base + 64 + (task & 1) * 16 + col0;
-          tmem_ld<NHW>(taddr, o);
-#pragma unroll
-          for (int i = 0; i < NHW; ++i) {
-            const float mn = fmaxf(m_ref[i], tmax[i]);
-            const float alpha = ex2(m_ref[i] - mn);
-            o[i] *= alpha;
-            lsum[i] *= alpha;
-            m_ref[i] = mn;
-          }
-          tmem_st<NHW>(taddr, o);
+          if (!rescale(a, ms, tmem + lane_base + 64 + (task & 1) * 16 + col0, tile, tmax, m_ref, lsum)) return;
         }
       }
       // ---- P = 2^(x - m): this group's heads of the token's 16-head row of the B operand

@@ -436,6 +436,10 @@ __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const sgld_plan_buffers& p = a.p;
   const int bcap = a.bcap, G = a.groups, W = a.workers;
+  // Launched as a programmatic dependent of the preceding kernel (the previous step's
+  // merge, which still reads counts / error): the block is resident early, and waits here
+  // for that kernel's completion before reading its inputs or writing any plan buffer.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // The decode launched after this plan may start its prologue now (programmatic
   // dependent launch); it waits for this grid's completion before reading the plan.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -636,8 +640,17 @@ cudaError_t launch_plan(const PlanLaunch& a, cudaStream_t stream) {
       configured[device] = ctx;
     }
   }
-  plan_kernel<<<1, kThreads, smem, stream>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, plan_kernel, a);
 }
 
 }  // namespace sgld
