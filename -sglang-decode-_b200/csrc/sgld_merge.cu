@@ -38,9 +38,6 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) merge_kernel(
     const float* __restrict__ partial, const float* __restrict__ lse, const int32_t* __restrict__ counts,
     const int32_t* __restrict__ error, T* __restrict__ out, int bcap, int hq, int d_dim, int smax) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // The next step's plan build (a programmatic dependent) may become resident now; it waits
-  // for this grid to complete before it touches the plan buffers this kernel reads.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);   // (request, head)
   const int lane = threadIdx.x & 31;
   if (row >= bcap * hq) return;
