@@ -118,12 +118,20 @@ bool encode_q_map(CUtensorMap* map, const void* base, int32_t dtype, int64_t d, 
 }
 
 // Kernel choice.  SGLD_DECODE_KERNEL=tcgen05 selects the tcgen05 kernel wherever it applies,
-// =mma the mma.sync kernel everywhere; unset, the measured-faster kernel for the geometry is
-// used (currently the mma.sync kernel: see the decode kernels' design notes).
-bool use_tc_kernel() {
+// =small the small-batch kernel wherever it applies, =mma the persistent mma.sync kernel
+// everywhere; unset, the measured-faster kernel for the geometry: the small-batch kernel when
+// the whole task capacity is at most kSmallTaskCapacity, else the persistent mma.sync kernel.
+constexpr int64_t kSmallTaskCapacity = 1024;
+
+bool kernel_env_is(const char* name) {
   const char* v = std::getenv("SGLD_DECODE_KERNEL");
-  return v != nullptr && std::strcmp(v, "tcgen05") == 0;
+  return v != nullptr && std::strcmp(v, name) == 0;
 }
+bool kernel_env_unset() {
+  const char* v = std::getenv("SGLD_DECODE_KERNEL");
+  return v == nullptr || v[0] == 0;
+}
+bool use_tc_kernel() { return kernel_env_is("tcgen05"); }
 
 bool tma_disabled_by_env() {
   const char* v = std::getenv("SGLD_DISABLE_TMA");
@@ -315,6 +323,11 @@ int prepare_launch(const sgld_decode_args& d, const sgld_plan_buffers* plan, con
     }
     return SGLD_KERNEL_TCGEN05;
   }
+  // Small-batch kernel: one CTA per task of the capacity (head_dim 128, 16-bit K/V, group <= 8).
+  const int64_t task_capacity = static_cast<int64_t>(geometry->batch_capacity) * geometry->max_splits * d.kv_heads;
+  if (!kv_fp8 && d.head_dim == 128 && group <= 8 && fast_kv && a.fast_q && task_capacity <= (int64_t{1} << 20) &&
+      (kernel_env_is("small") || (kernel_env_unset() && task_capacity <= kSmallTaskCapacity)))
+    return SGLD_KERNEL_SMALL;
   // mma.sync kernel.  Paged KV by tensor-map TMA: a box of 32 tokens never crosses a page
   // because stages start 32-token aligned and 32 divides the page size.  Smaller pages stay
   // on the multi-warp cp.async path, which measured faster than 8- or 16-row boxes.  So do
@@ -381,8 +394,9 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
     e = sgld::launch_kv_write(kw, st, true);
     if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent KV-cache write launch");
   }
-  e = (kind == SGLD_KERNEL_TCGEN05 || kind == SGLD_KERNEL_TCGEN05_TMA) ? sgld::launch_decode_tc(a, st)
-                                                                        : sgld::launch_decode(a, st);
+  if (kind == SGLD_KERNEL_TCGEN05 || kind == SGLD_KERNEL_TCGEN05_TMA) e = sgld::launch_decode_tc(a, st);
+  else if (kind == SGLD_KERNEL_SMALL) e = sgld::launch_decode_small(a, st);
+  else e = sgld::launch_decode(a, st);
   if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent launch");
   e = sgld::launch_merge(d.partial, d.lse, plan->counts, plan->error, d.out, d.dtype, geometry->batch_capacity,
                          d.query_heads, d.head_dim, geometry->max_splits, st, true);

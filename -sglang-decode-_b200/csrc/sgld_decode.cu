@@ -202,6 +202,79 @@ struct Kernel {
     }
   }
 
+  // R0 / R1 (static stride W): the tasks a CTA will claim are known in advance (worker,
+  // worker + W, ...), so lanes 0..kLook-1 of the scheduler warp resolve the next kLook tasks
+  // in parallel (each a chain of dependent global loads: order, record fields, request
+  // counts / indptr) and lane 0 pushes them in claim order.  The serial claim loop costs
+  // those round trips once per task, which dominates small batches.
+  static constexpr int kLook = 4;
+
+  __device__ static void scheduler_strided(const DecodeLaunch& a, Misc& ms, int mode) {
+    const sgld_plan_buffers& p = a.p;
+    const int lane = threadIdx.x & 31;
+    const int G = a.d.kv_heads;
+    const int W = gridDim.x;
+    const int total = *p.record_count * G;
+    int ti = 0;
+    uint32_t tph = 0;
+    bool ok = true;
+    for (int base = blockIdx.x; ok && base < total; base += kLook * W) {
+      const int task = base + lane * W;
+      TaskDesc t{};
+      t.valid = 0;
+      if (lane < kLook && task < total) {
+        t.group = task % G;
+        int record = task / G;
+        if (mode == 0) {   // attention.py:25-39 -- upper-bound search over offsets
+          int lo = 0, hi = *p.active;
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (record >= p.offsets[mid + 1]) lo = mid + 1;
+            else hi = mid;
+          }
+          t.request = lo;
+          t.split = record - p.offsets[lo];
+          const int chunk = p.chunk[lo];
+          t.begin = t.split * chunk;
+          t.end = min(t.begin + chunk, p.lengths[lo]);
+        } else {           // attention.py:41-47
+          record = p.order[record];
+          t.request = p.request[record];
+          t.split = p.split[record];
+          t.begin = p.begin[record];
+          t.end = p.end[record];
+        }
+        // never produced by a valid plan; skipping keeps every access in bounds
+        if (!(t.request < 0 || t.request >= a.bcap || t.end <= t.begin || t.split < 0 || t.split >= a.smax)) {
+          t.count_r = p.counts[t.request];
+          t.base = a.csr ? a.d.indptr[t.request] : t.request;
+          t.valid = 1;
+          if (a.fast_q && t.request < a.q_rows) prefetch_q(a, t);
+        }
+      }
+      for (int l = 0; l < kLook; ++l) {
+        TaskDesc u;
+        u.request = __shfl_sync(0xffffffffu, t.request, l);
+        u.split = __shfl_sync(0xffffffffu, t.split, l);
+        u.group = __shfl_sync(0xffffffffu, t.group, l);
+        u.begin = __shfl_sync(0xffffffffu, t.begin, l);
+        u.end = __shfl_sync(0xffffffffu, t.end, l);
+        u.count_r = __shfl_sync(0xffffffffu, t.count_r, l);
+        u.base = __shfl_sync(0xffffffffu, t.base, l);
+        u.valid = __shfl_sync(0xffffffffu, t.valid, l);
+        if (u.valid && lane == 0) ok = push_task(ms, ti, tph, u, a.d.status);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+      }
+    }
+    if (lane == 0) {
+      TaskDesc end_marker{};
+      end_marker.valid = 0;
+      push_task(ms, ti, tph, end_marker, a.d.status);
+    }
+    __syncwarp();
+  }
+
   __device__ static void scheduler(const DecodeLaunch& a, Misc& ms) {
     const sgld_plan_buffers& p = a.p;
     const int G = a.d.kv_heads;
@@ -937,8 +1010,13 @@ struct Kernel {
     } else if (warp == C::kIndexerWarp) {
       indexer(a, smem, ms);
     } else {
-      if (lane == 0) scheduler(a, ms);
-      __syncwarp();
+      const int mode = *a.p.mode;
+      if (mode <= 1) {
+        scheduler_strided(a, ms, mode);
+      } else {
+        if (lane == 0) scheduler(a, ms);
+        __syncwarp();
+      }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
@@ -993,6 +1071,265 @@ cudaError_t launch_typed(const DecodeLaunch& a, cudaStream_t stream) {
   return cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NT, F8>, a);
 }
 
+// ------------------------------------------------------------------ small-batch kernel
+// One CTA of four warps per task, for geometries whose whole task capacity
+// (Bcap * Smax * Hkv) fits in a few waves (a handful of short requests, e.g. 8 requests of
+// up to 1K tokens).  There is no persistent pipeline: each CTA resolves its task from the plan
+// (attention.py:23-47, R0 prefix search or the record arrays; the dispatch order of a mode
+// does not change a task's arithmetic), gathers the task's indices and K/V rows with cp.async
+// in 64-token stages, and runs the persistent kernel's fragment code on them
+// (qk_tile / pv_tile, the same online softmax and the same four-warp combine), so a task of
+// one stage gives the same bits on both kernels.  Tasks past the plan's count exit at once.
+template <typename T>
+struct Small {
+  using K = Kernel<T, 128, 1, false>;
+  using C = Cfg<128, 1, false>;
+  static constexpr int D = 128;
+  static constexpr int kThreads = 128;                  // four warps, 16 rows of a stage each
+  static constexpr int kTS = C::kTS;                    // 64 tokens per stage
+  // One stage buffer (K and V, 32 KB): with about 36 KB a CTA, registers (122 a thread) rather
+  // than shared memory bound the CTAs per SM (four), so a small batch's tasks run in one wave.
+  static constexpr int kOffQ = C::kStageBytes;
+  static constexpr int kOffIdx = kOffQ + C::kQBytes;    // koff / voff of the stage
+  static constexpr int kOffMl = kOffIdx + 2 * kTS * 8;
+  static constexpr int kSmemUsed = kOffMl + 2 * 4 * 8 * 4;
+  static constexpr int kSmemBytes = kSmemUsed + 1024;
+  static_assert(4 * C::kQRows * C::kRedStride * 4 <= C::kStageBytes, "the combine reuses stage 0");
+
+  // Index loads and cp.async of the stage starting at token t0.
+  __device__ static void load_stage(const DecodeLaunch& a, unsigned char* smem, const TaskDesc& t, int t0) {
+    const int tid = threadIdx.x;
+    int64_t* koff = reinterpret_cast<int64_t*>(smem + kOffIdx);
+    int64_t* voff = koff + kTS;
+    if (tid < kTS) {
+      const int tok = min(t0 + tid, t.end - 1);
+      int64_t phys, inner = 0;
+      if (a.csr) {
+        phys = __ldg(a.d.pages + t.base + tok);
+      } else {
+        const int page = tok / a.d.page_size;
+        phys = __ldg(a.d.pages + static_cast<int64_t>(t.base) * a.d.pt_stride[0] +
+                     static_cast<int64_t>(page) * a.d.pt_stride[1]);
+        inner = tok - page * a.d.page_size;
+      }
+      koff[tid] = phys * a.d.k_stride[0] + inner * a.d.k_stride[1] + static_cast<int64_t>(t.group) * a.d.k_stride[2];
+      voff[tid] = phys * a.d.v_stride[0] + inner * a.d.v_stride[1] + static_cast<int64_t>(t.group) * a.d.v_stride[2];
+    }
+    __syncthreads();
+    const int ntok = min(kTS, t.end - t0);
+    const T* kb = static_cast<const T*>(a.d.k);
+    const T* vb = static_cast<const T*>(a.d.v);
+    const uint32_t kdst = smem_addr(smem);
+    const uint32_t vdst = kdst + C::kTileBytes;
+    const int c = tid & 15;
+#pragma unroll
+    for (int j = tid >> 4; j < kTS; j += kThreads / 16) {
+      const bool live = j < ntok;
+      const uint32_t off = tile_off<kTS>(j, c);
+      cp_async_16_fill(kdst + off, live ? kb + koff[j] + c * 8 : kb, live ? 16u : 0u);
+      cp_async_16_fill(vdst + off, live ? vb + voff[j] + c * 8 : vb, live ? 16u : 0u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+
+  __device__ static void run(const DecodeLaunch& a) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const sgld_plan_buffers& p = a.p;
+    const int G = a.d.kv_heads;
+    const int task = blockIdx.x;
+    const int mode = *p.mode;
+    if (task >= *p.record_count * G) return;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g8 = lane >> 2, t4 = lane & 3;
+    TaskDesc t;
+    t.group = task % G;
+    const int record = task / G;
+    if (mode == 0) {   // attention.py:25-39 -- upper-bound search over offsets
+      int lo = 0, hi = *p.active;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (record >= p.offsets[mid + 1]) lo = mid + 1;
+        else hi = mid;
+      }
+      t.request = lo;
+      t.split = record - p.offsets[lo];
+      const int chunk = p.chunk[lo];
+      t.begin = t.split * chunk;
+      t.end = min(t.begin + chunk, p.lengths[lo]);
+    } else {           // every record once; the mode's order does not change a task's result
+      t.request = p.request[record];
+      t.split = p.split[record];
+      t.begin = p.begin[record];
+      t.end = p.end[record];
+    }
+    if (t.request < 0 || t.request >= a.bcap || t.end <= t.begin || t.split < 0 || t.split >= a.smax) return;
+    t.base = a.csr ? a.d.indptr[t.request] : t.request;
+    // ---- query group (rows past the group, or a request past q's rows, read as zeros)
+    const int gs = a.group_size;
+    const bool in_q = t.request < a.q_rows;
+    if (!in_q && tid == 0) atomicOr(a.d.status, kStatusQRows);
+    {
+      const int r = tid >> 4, c = tid & 15;   // 8 rows x 16 chunks: one copy per thread
+      const bool live = in_q && r < gs;
+      const T* src = static_cast<const T*>(a.d.q) + static_cast<int64_t>(in_q ? t.request : 0) * a.d.q_stride[0] +
+                     static_cast<int64_t>(t.group * gs + (live ? r : 0)) * a.d.q_stride[1] + c * 8;
+      cp_async_16_fill(smem_addr(smem + kOffQ) + tile_off<C::kQRows>(r, c), src, live ? 16u : 0u);
+    }
+    load_stage(a, smem, t, t.begin);   // commits the query copies with the first stage
+    const float cap = a.d.logit_cap;
+    const bool capped = cap > 0.f;
+    const float sc = (capped ? a.d.scale : a.d.scale * kLog2e) * a.d.k_scale;
+    const float cap_log2e = cap * kLog2e, two_log2e_over_cap = capped ? 2.f * kLog2e / cap : 0.f;
+    constexpr int KS = D / 16;
+    uint32_t qf[1][KS][2];
+    float o[KS][1][4];
+    float m[1][2], lsum[1][2];
+    m[0][0] = m[0][1] = -INFINITY;
+    lsum[0][0] = lsum[0][1] = 0.f;
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) o[mt][0][0] = o[mt][0][1] = o[mt][0][2] = o[mt][0][3] = 0.f;
+    const int row0 = warp * 16;
+    for (int t0 = t.begin; t0 < t.end; t0 += kTS) {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      __syncthreads();
+      if (t0 == t.begin) {
+        const uint32_t qbase = smem_addr(smem + kOffQ);
+#pragma unroll
+        for (int ks = 0; ks < KS; ks += 2) {
+          const int row = lane & 7;
+          const int chunk = 2 * ks + (lane >> 3);
+          ldsm_x4(qbase + tile_off<C::kQRows>(row, chunk), qf[0][ks][0], qf[0][ks][1], qf[0][ks + 1][0], qf[0][ks + 1][1]);
+        }
+      }
+      const int valid = min(kTS, t.end - t0) - row0;
+      if (valid > 0) {
+        const uint32_t kb = smem_addr(smem);
+        float sv[1][4];
+        K::qk_tile(kb, row0, qf, sv);
+        uint32_t pb[1][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int tok = g8 + (i >= 2 ? 8 : 0);
+          float x = sv[0][i] * sc;
+          if (capped) x = cap_log2e * (1.f - 2.f / (ex2(x * two_log2e_over_cap) + 1.f));
+          sv[0][i] = tok < valid ? x : -INFINITY;
+        }
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          float mx = fmaxf(sv[0][jj], sv[0][jj + 2]);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float mnew = fmaxf(m[0][jj], mx);
+          const float alpha = ex2(m[0][jj] - mnew);
+          const float p0 = ex2(sv[0][jj] - mnew), p1 = ex2(sv[0][jj + 2] - mnew);
+          sv[0][jj] = p0;
+          sv[0][jj + 2] = p1;
+          lsum[0][jj] = lsum[0][jj] * alpha + (p0 + p1);
+          m[0][jj] = mnew;
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            o[mt][0][jj] *= alpha;
+            o[mt][0][jj + 2] *= alpha;
+          }
+        }
+        pb[0][0] = movmatrix_t(Mma<T>::pack(sv[0][0], sv[0][1]));
+        pb[0][1] = movmatrix_t(Mma<T>::pack(sv[0][2], sv[0][3]));
+        K::pv_tile(kb + C::kTileBytes, row0, valid, pb, o);
+      }
+      __syncthreads();   // every warp is done with the stage before it is refilled
+      if (t0 + kTS < t.end) load_stage(a, smem, t, t0 + kTS);
+    }
+    // ---- combine the four warps (the persistent kernel's epilogue order) and store
+    float* red = reinterpret_cast<float*>(smem);   // the stage buffer is free now
+    float* ms_m = reinterpret_cast<float*>(smem + kOffMl);
+    float* ms_l = ms_m + 4 * 8;
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      float l = lsum[0][jj];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      if (g8 == 0) {
+        ms_m[warp * 8 + 2 * t4 + jj] = m[0][jj];
+        ms_l[warp * 8 + 2 * t4 + jj] = l;
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int d = mt * 16 + g8 + (i >= 2 ? 8 : 0);
+        const int head = 2 * t4 + (i & 1);
+        red[(warp * C::kQRows + head) * C::kRedStride + d] = o[mt][0][i];
+      }
+    __syncthreads();
+    const int64_t slot0 = (static_cast<int64_t>(t.request) * a.d.query_heads + t.group * gs) * a.smax + t.split;
+    constexpr int D4 = D / 4;
+    for (int idx = tid; idx < gs * D4; idx += kThreads) {
+      const int head = idx / D4, d = (idx - head * D4) * 4;
+      float sw[4];
+      float gm = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        sw[w] = ms_m[w * 8 + head];
+        gm = fmaxf(gm, sw[w]);
+      }
+      float gl = 0.f;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        sw[w] = sw[w] == -INFINITY ? 0.f : ex2(sw[w] - gm);
+        gl += ms_l[w * 8 + head] * sw[w];
+        const float4 r = *reinterpret_cast<const float4*>(red + (w * C::kQRows + head) * C::kRedStride + d);
+        v.x += r.x * sw[w];
+        v.y += r.y * sw[w];
+        v.z += r.z * sw[w];
+        v.w += r.w * sw[w];
+      }
+      const float vs = a.d.v_scale;
+      const float4 res = make_float4(v.x / gl * vs, v.y / gl * vs, v.z / gl * vs, v.w / gl * vs);
+      const int64_t slot = slot0 + static_cast<int64_t>(head) * a.smax;
+      *reinterpret_cast<float4*>(a.d.partial + slot * D + d) = res;
+      if (d == 0) a.d.lse[slot] = (gm + lg2(gl)) * kLn2;
+    }
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(Small<T>::kThreads, 4) decode_small_kernel(const __grid_constant__ DecodeLaunch a) {
+  Small<T>::run(a);
+}
+
+template <typename T>
+cudaError_t launch_small(const DecodeLaunch& a, cudaStream_t stream) {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<void*> configured[kMaxDevices] = {};
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+  void* ctx = current_context();
+  if (ctx == nullptr || configured[device].load(std::memory_order_acquire) != ctx) {
+    e = cudaFuncSetAttribute(decode_small_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Small<T>::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured[device].store(ctx, std::memory_order_release);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.bcap * a.smax * a.d.kv_heads));   // the task capacity
+  cfg.blockDim = dim3(Small<T>::kThreads);
+  cfg.dynamicSmemBytes = Small<T>::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_small_kernel<T>, a);
+}
+
 template <typename T>
 cudaError_t launch_dtype(const DecodeLaunch& a, cudaStream_t stream) {
   const bool wide = a.group_size > 8;
@@ -1012,6 +1349,10 @@ cudaError_t launch_dtype(const DecodeLaunch& a, cudaStream_t stream) {
 
 cudaError_t launch_decode(const DecodeLaunch& a, cudaStream_t stream) {
   return a.d.dtype == SGLD_DTYPE_BF16 ? launch_dtype<__nv_bfloat16>(a, stream) : launch_dtype<__half>(a, stream);
+}
+
+cudaError_t launch_decode_small(const DecodeLaunch& a, cudaStream_t stream) {
+  return a.d.dtype == SGLD_DTYPE_BF16 ? launch_small<__nv_bfloat16>(a, stream) : launch_small<__half>(a, stream);
 }
 
 }  // namespace sgld

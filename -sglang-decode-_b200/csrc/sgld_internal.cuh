@@ -68,6 +68,9 @@ struct KVWrite {
 cudaError_t launch_kv_write(const KVWrite& kv, cudaStream_t stream, bool programmatic);
 
 cudaError_t launch_decode(const DecodeLaunch& a, cudaStream_t stream);
+// Small-batch kernel: one CTA per task of the capacity (head_dim 128, 16-bit K/V, group <= 8,
+// 16-byte aligned K/V and Q rows).
+cudaError_t launch_decode_small(const DecodeLaunch& a, cudaStream_t stream);
 // tcgen05 kernel (head_dim 128, 16-bit K/V, 16-byte aligned rows, qmap encoded).
 cudaError_t launch_decode_tc(const DecodeLaunch& a, cudaStream_t stream);
 

@@ -57,7 +57,7 @@ EXPORTS = ("sgld_abi_version", "sgld_last_error", "sgld_layer_workspace_bytes", 
            "sgld_decode_persistent", "sgld_merge_splits", "sgld_decode_persistent_noalloc",
            "sgld_decode_kernel_kind")
 ABI_VERSION = 8
-KERNEL_KINDS = {0: "mma.sync", 1: "tcgen05", 2: "tcgen05+tma", 3: "mma.sync+tma"}
+KERNEL_KINDS = {0: "mma.sync", 1: "tcgen05", 2: "tcgen05+tma", 3: "mma.sync+tma", 4: "small"}
 
 _lock = threading.Lock()
 _lib = None

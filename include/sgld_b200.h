@@ -196,15 +196,19 @@ enum {
   SGLD_KERNEL_MMA_SYNC = 0,      /* mma.sync kernel, cp.async or element copies of K/V rows        */
   SGLD_KERNEL_TCGEN05 = 1,       /* tcgen05.mma kernel, TMEM accumulators, cp.async K/V rows        */
   SGLD_KERNEL_TCGEN05_TMA = 2,   /* tcgen05.mma kernel, paged K/V by tensor-map TMA boxes           */
-  SGLD_KERNEL_MMA_SYNC_TMA = 3   /* mma.sync kernel, paged K/V by tensor-map TMA boxes              */
+  SGLD_KERNEL_MMA_SYNC_TMA = 3,  /* mma.sync kernel, paged K/V by tensor-map TMA boxes              */
+  SGLD_KERNEL_SMALL = 4          /* small-batch kernel: one CTA per task of the task capacity       */
 };
 
 /*
  * Which decode kernel sgld_decode_persistent would launch for these arguments (an
  * SGLD_KERNEL_* value), or minus an sgld_status when the arguments are invalid.  Nothing is
- * enqueued.  The tcgen05 kernel serves head_dim 128 with 16-bit K/V in 16-byte aligned rows
- * and a Q whose rows are 16-byte aligned; other geometries use the mma.sync kernel.  No
- * counterpart in the reference (its only kernel is the Triton one).
+ * enqueued.  By default a geometry whose task capacity (batch_capacity * max_splits *
+ * kv_heads) is at most 1024 uses the small-batch kernel (head_dim 128, 16-bit K/V, group <= 8,
+ * 16-byte aligned rows) and every other one the persistent mma.sync kernel; the environment
+ * variable SGLD_DECODE_KERNEL=mma|small|tcgen05 forces a kernel where it applies (the tcgen05
+ * kernel: head_dim 128, 16-bit K/V, 16-byte aligned rows).  No counterpart in the reference
+ * (its only kernel is the Triton one).
  */
 int sgld_decode_kernel_kind(const sgld_decode_args* args, const sgld_plan_buffers* plan,
                             const sgld_plan_geometry* geometry);

@@ -1,13 +1,17 @@
-"""Both decode kernels against the FP32 oracle: the mma.sync kernel and the tcgen05 kernel
-(QK and PV on tcgen05.mma with tensor-memory accumulators, head_dim 128, 16-bit K/V).
+"""Every decode kernel against the FP32 oracle: the persistent mma.sync kernel, the small-batch
+kernel (one CTA per task) and the tcgen05 kernel (QK and PV on tcgen05.mma with tensor-memory
+accumulators, head_dim 128, 16-bit K/V).
 
-SGLD_DECODE_KERNEL selects the kernel per call ("mma" / "tcgen05"); each case asserts which
-kernel actually ran (sgld_decode_kernel_kind), so a silent fallback cannot pass for coverage.
+SGLD_DECODE_KERNEL selects the kernel per call ("mma" / "small" / "tcgen05"); each case asserts
+which kernel actually ran (sgld_decode_kernel_kind), so a silent fallback cannot pass for
+coverage (the small-batch kernel serves groups of at most 8).
 Tolerance: max-abs 2e-2, mean-abs 2e-3 against FP32; every dispatch mode bit-identical.
 """
+import numpy as np
 import pytest
 import torch
 
+from oracle import attention as A
 from sglang_decode.config import DecodeConfig, Mode
 from sglang_decode.runtime.engine import DecodeEngine
 from sglang_decode.workloads import baseline, generate, make_csr_inputs, make_inputs, subset, update_plan
@@ -15,7 +19,12 @@ from tests.helpers import assert_rows_within_tolerance, assert_within_tolerance,
 
 pytestmark = pytest.mark.gpu
 
-KERNELS = {"mma": {"mma.sync", "mma.sync+tma"}, "tcgen05": {"tcgen05", "tcgen05+tma"}}
+KERNELS = {"mma": {"mma.sync", "mma.sync+tma"}, "small": {"small"}, "tcgen05": {"tcgen05", "tcgen05+tma"}}
+
+
+def _expect(kernel, group=8):
+    """Kernels a call may take: the small-batch kernel only serves groups of at most 8."""
+    return KERNELS["mma"] if kernel == "small" and group > 8 else KERNELS[kernel]
 
 
 @pytest.fixture(params=sorted(KERNELS))
@@ -49,7 +58,7 @@ def test_csr_groups(kernel, dtype, group):
     for mode in Mode:
         engine = DecodeEngine(c, dtype=dtype, force_mode=mode)
         out = _run(engine, (q, k, v, idx), lengths, indptr=indptr)
-        assert engine.kernel_kind() in KERNELS[kernel]
+        assert engine.kernel_kind() in _expect(kernel, group)
         assert_within_tolerance(out, expected, len(lengths))
         outs.append(out.clone())
     assert all(torch.equal(outs[0], o) for o in outs[1:]), "every mode gives the same bits"
@@ -126,3 +135,49 @@ def test_baseline_shapes_on_the_tcgen05_kernel(monkeypatch, name):
         assert_rows_within_tolerance(out, expected, range(len(b.lengths)))
         outs.append(out.clone())
     assert all(torch.equal(outs[0], o) for o in outs[1:])
+
+
+@pytest.mark.parametrize("window_left", [0, 63, 500, 4096])
+def test_sliding_window_csr(kernel, window_left):
+    """SGLang / FlashInfer window_left: the query attends to the last min(L, window_left + 1)
+    tokens; the window is the unchanged kernel on shifted CSR bases and windowed lengths."""
+    from sglang_decode.window import window_bases, window_lengths
+    lengths = [1, 65, 300, 0, 1000, 129]
+    c = DecodeConfig(batch_capacity=8, max_splits=8, max_context=1024, query_heads=16, kv_heads=2, head_dim=128,
+                     page_size=1, workers=37)
+    q, k, v, idx, indptr = (t.cuda() for t in make_csr_inputs(c, lengths, device="cpu", pool=4000))
+    full = torch.tensor(lengths, dtype=torch.int32, device="cuda")
+    wl = window_lengths(lengths, window_left)
+    bases = window_bases(indptr, full, window_left)
+    starts = indptr.cpu().tolist()
+    want = np.zeros((len(lengths), c.query_heads, c.head_dim), dtype=np.float32)
+    for r, (n, w) in enumerate(zip(lengths, wl)):
+        if w:
+            rows = idx[starts[r] + n - w:starts[r] + n].long()
+            want[r] = A.request_attention(q[r].float().cpu().numpy(), k[rows].float().cpu().numpy(),
+                                          v[rows].float().cpu().numpy())
+    engine = DecodeEngine(c, force_mode=Mode.D4)
+    out = _run(engine, (q, k, v, idx), wl, indptr=bases)
+    assert engine.kernel_kind() in KERNELS[kernel]
+    assert_within_tolerance(out, want, len(lengths))
+
+
+def test_small_kernel_is_bitwise_equal_to_the_persistent_kernel_on_single_stage_tasks(monkeypatch):
+    """C1's tasks are at most 64 tokens (one stage): the small-batch kernel runs the persistent
+    kernel's fragment code, softmax and combine on them, so the outputs agree bit for bit."""
+    b = baseline("C1", workers=torch.cuda.get_device_properties(0).multi_processor_count)
+    data = generate(b, device="cuda", seed=17)
+    outs = {}
+    for kernel in ("mma", "small"):
+        monkeypatch.setenv("SGLD_DECODE_KERNEL", kernel)
+        engine = DecodeEngine(b.config, device="cuda", dtype=b.dtype)
+        update_plan(engine, b.lengths, b.splits)
+        engine.prepare()
+        out = engine.execute(data["q"], data["k"], data["v"], data["pages"], indptr=data["indptr"])
+        torch.cuda.synchronize()
+        assert engine.layers[0].status.item() == 0
+        assert engine.kernel_kind() in KERNELS[kernel]
+        n = engine.plan.record_count.item()
+        assert (engine.plan.end[:n] - engine.plan.begin[:n]).max().item() <= 64
+        outs[kernel] = out.clone()
+    assert torch.equal(outs["mma"], outs["small"])
