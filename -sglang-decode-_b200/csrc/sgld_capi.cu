@@ -143,7 +143,7 @@ int check_plan_pointers(const sgld_plan_buffers* p) {
   const void* ptrs[] = {p->lengths, p->splits, p->active, p->counts, p->offsets, p->chunk,
                         p->request, p->split, p->begin, p->end, p->weight, p->order,
                         p->pack_first, p->pack_count, p->record_count, p->num_packs, p->mode,
-                        p->error, p->static_head, p->static_next};
+                        p->error, p->static_head, p->static_next, p->arrivals};
   for (const void* q : ptrs)
     if (q == nullptr) return fail(SGLD_ERR_INVALID_ARGUMENT, "a plan buffer pointer is NULL");
   return SGLD_OK;
@@ -171,6 +171,46 @@ size_t sgld_layer_workspace_bytes(int32_t batch_capacity, int32_t query_heads, i
          + slots * head_dim * sizeof(float)                    /* partial */
          + slots * sizeof(float)                               /* lse */
          + sizeof(int32_t);                                    /* status */
+}
+
+size_t sgld_plan_storage_words(const sgld_plan_geometry* g) {
+  if (g == nullptr || g->batch_capacity <= 0 || g->max_splits <= 0 || g->groups <= 0 || g->workers <= 0) return 0;
+  const size_t b = static_cast<size_t>(g->batch_capacity), e = b * g->max_splits, t = e * g->groups;
+  return 5 * b + 2 + 6 * e + 3 * t + 4 + static_cast<size_t>(g->workers) + b * g->groups;   // sizes as listed below
+}
+
+int sgld_plan_buffers_in_storage(int32_t* storage, const sgld_plan_geometry* g, sgld_plan_buffers* out) {
+  if (storage == nullptr || out == nullptr || sgld_plan_storage_words(g) == 0)
+    return fail(SGLD_ERR_INVALID_ARGUMENT, "storage, geometry or output is NULL or empty");
+  const size_t b = static_cast<size_t>(g->batch_capacity), e = b * g->max_splits, t = e * g->groups;
+  int32_t* cur = storage;
+  auto take = [&cur](size_t n) {
+    int32_t* p = cur;
+    cur += n;
+    return p;
+  };
+  out->lengths = take(b);
+  out->splits = take(b);
+  out->active = take(1);
+  out->counts = take(b);
+  out->offsets = take(b + 1);
+  out->chunk = take(b);
+  out->request = take(e);
+  out->split = take(e);
+  out->begin = take(e);
+  out->end = take(e);
+  out->weight = take(e);
+  out->order = take(e);
+  out->pack_first = take(t);
+  out->pack_count = take(t);
+  out->record_count = take(1);
+  out->num_packs = take(1);
+  out->mode = take(1);
+  out->error = take(1);
+  out->static_head = take(static_cast<size_t>(g->workers));
+  out->static_next = take(t);
+  out->arrivals = take(b * g->groups);
+  return SGLD_OK;
 }
 
 int sgld_plan_build(const sgld_plan_buffers* plan, const sgld_plan_geometry* geometry,
@@ -398,6 +438,7 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   else if (kind == SGLD_KERNEL_SMALL) e = sgld::launch_decode_small(a, st);
   else e = sgld::launch_decode(a, st);
   if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent launch");
+  if (kind == SGLD_KERNEL_SMALL) return SGLD_OK;   // the small-batch kernel merges the splits itself
   e = sgld::launch_merge(d.partial, d.lse, plan->counts, plan->error, d.out, d.dtype, geometry->batch_capacity,
                          d.query_heads, d.head_dim, geometry->max_splits, st, true);
   if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent merge launch");

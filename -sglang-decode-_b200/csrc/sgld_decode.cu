@@ -45,6 +45,7 @@
 #include <type_traits>
 
 #include "sgld_internal.cuh"
+#include "sgld_merge.cuh"
 #include "sgld_ptx.cuh"
 
 namespace sgld {
@@ -1080,6 +1081,9 @@ cudaError_t launch_typed(const DecodeLaunch& a, cudaStream_t stream) {
 // in 64-token stages, and runs the persistent kernel's fragment code on them
 // (qk_tile / pv_tile, the same online softmax and the same four-warp combine), so a task of
 // one stage gives the same bits on both kernels.  Tasks past the plan's count exit at once.
+// The split merge is fused: the last split CTA of a (request, KV head) to finish merges that
+// group's rows (merge_row4, the merge kernel's arithmetic), counting arrivals in the plan's
+// `arrivals` words, so a step is two launches (plan, decode) instead of three.
 template <typename T>
 struct Small {
   using K = Kernel<T, 128, 1, false>;
@@ -1140,7 +1144,19 @@ struct Small {
     const int G = a.d.kv_heads;
     const int task = blockIdx.x;
     const int mode = *p.mode;
-    if (task >= *p.record_count * G) return;
+    const bool plan_error = *p.error != 0;
+    // ---- rows the fused merge never reaches, by merge_kernel's rules: a request without
+    // splits is zero, and every row is NaN when the plan's error word is set (the plan then
+    // has no records).  CTA r*G+g covers request r's query heads of KV head g.
+    if (task < a.bcap * G) {
+      const int r = task / G, g = task - r * G;
+      if (plan_error || p.counts[r] == 0) {
+        const T fill = from_float<T>(plan_error ? __int_as_float(0x7fc00000) : 0.f);
+        T* orow = static_cast<T*>(a.d.out) + (static_cast<int64_t>(r) * a.d.query_heads + g * a.group_size) * D;
+        for (int i = threadIdx.x; i < a.group_size * D; i += kThreads) orow[i] = fill;
+      }
+    }
+    if (plan_error || task >= *p.record_count * G) return;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g8 = lane >> 2, t4 = lane & 3;
     TaskDesc t;
@@ -1295,6 +1311,31 @@ struct Small {
       *reinterpret_cast<float4*>(a.d.partial + slot * D + d) = res;
       if (d == 0) a.d.lse[slot] = (gm + lg2(gl)) * kLn2;
     }
+    // ---- fused merge: the last of the request's split CTAs of this KV head to arrive merges
+    // the group's rows with merge_row4 (the stand-alone merge kernel's arithmetic, so the
+    // output has the same bits) and leaves the arrival counter at zero for the next decode.
+    // Release: every thread fences its partial/LSE stores before the arrival; acquire: the
+    // last CTA fences after it and reads the slots through L2.
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    int* arrival = p.arrivals + static_cast<int64_t>(t.request) * G + t.group;
+    const int n_splits = p.counts[t.request];
+    if (tid == 0) s_last = atomicAdd(arrival, 1) == n_splits - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int idx = tid; idx < gs * D4; idx += kThreads) {
+      const int head = idx / D4, d = (idx - head * D4) * 4;
+      const int64_t row = static_cast<int64_t>(t.request) * a.d.query_heads + t.group * gs + head;
+      const float4 r = merge_row4(a.d.partial + row * a.smax * D + d, a.d.lse + row * a.smax, n_splits, D);
+      T* o = static_cast<T*>(a.d.out) + row * D + d;
+      o[0] = from_float<T>(r.x);
+      o[1] = from_float<T>(r.y);
+      o[2] = from_float<T>(r.z);
+      o[3] = from_float<T>(r.w);
+    }
+    if (tid == 0) *arrival = 0;
   }
 };
 

@@ -1,12 +1,9 @@
 // Split merge -- the reference's merge_splits (kernels/merge.py:7-30).
 //
 // One warp per (request, query head), four head dims per lane (float4).  Per row:
-// the LSE-weighted merge of the first counts[request] split slots, in split order
-// (the recurrence m' = max(m, l_s), acc = acc*e^(m-m') + p_s*e^(l_s-m'), same for
-// the denominator), output = acc / max(den, 1e-30); rows without splits are zero and
-// every output is NaN when the plan's error word is set.  Slots >= counts[request]
-// are never read (they may hold stale NaN).  The split loads of a row are issued
-// eight at a time so the merge costs a few memory round trips, not one per split.
+// merge_row4 (sgld_merge.cuh) over the first counts[request] split slots, in split order;
+// rows without splits are zero and every output is NaN when the plan's error word is set.
+// Slots >= counts[request] are never read (they may hold stale NaN).
 //
 // Launched right after the decode kernel with programmatic dependent launch: the
 // CTAs may start while the decode grid drains and wait (griddepcontrol.wait) until
@@ -16,14 +13,13 @@
 #include <cuda_runtime.h>
 
 #include "sgld_internal.cuh"
+#include "sgld_merge.cuh"
 #include "sgld_ptx.cuh"
 
 namespace sgld {
 namespace {
 
-constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kWarpsPerBlock = 4;
-constexpr int kUnroll = 8;
 
 template <typename T>
 __device__ __forceinline__ void store4(T* dst, float4 v) {
@@ -47,36 +43,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) merge_kernel(
   T* orow = out + static_cast<int64_t>(row) * d_dim;
   const int64_t base = static_cast<int64_t>(row) * smax;
   for (int d = lane * 4; d < d_dim; d += 128) {
-    float mm = -INFINITY, den = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s0 = 0; s0 < n; s0 += kUnroll) {
-      float l[kUnroll];
-      float4 p[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        if (s0 + u < n) {
-          l[u] = __ldcg(lse + base + s0 + u);
-          p[u] = __ldcg(reinterpret_cast<const float4*>(partial + (base + s0 + u) * d_dim + d));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        if (s0 + u < n) {
-          const float nm = fmaxf(mm, l[u]);
-          const float ow = ex2((mm - nm) * kLog2e);
-          const float w = ex2((l[u] - nm) * kLog2e);
-          acc.x = acc.x * ow + p[u].x * w;
-          acc.y = acc.y * ow + p[u].y * w;
-          acc.z = acc.z * ow + p[u].z * w;
-          acc.w = acc.w * ow + p[u].w * w;
-          den = den * ow + w;
-          mm = nm;
-        }
-      }
-    }
-    const float inv = 1.f / fmaxf(den, 1.0e-30f);
-    float4 r = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    if (n == 0) r = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 r = merge_row4(partial + base * d_dim + d, lse + base, n, d_dim);
     if (err) {
       const float q = __int_as_float(0x7fc00000);
       r = make_float4(q, q, q, q);

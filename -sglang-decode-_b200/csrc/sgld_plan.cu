@@ -489,6 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
     *p.error = error ? 1 : 0;
   }
   for (int i = tid; i < a.n_counters; i += kThreads) a.counters[i] = 0;
+  for (int i = tid; i < bcap * a.groups; i += kThreads) p.arrivals[i] = 0;   // fused-merge arrivals
 
   if (a.force == 0) {   // builder.py:11-14 -- R0 plans stop after count/scan
     if (tid == 0) {

@@ -23,7 +23,16 @@ class PlanGeometry(ctypes.Structure):
 
 PLAN_FIELDS = ("lengths", "splits", "active", "counts", "offsets", "chunk", "request", "split",
                "begin", "end", "weight", "order", "pack_first", "pack_count", "record_count",
-               "num_packs", "mode", "error", "static_head", "static_next")
+               "num_packs", "mode", "error", "static_head", "static_next", "arrivals")
+
+
+def plan_field_words(batch_capacity, max_splits, groups, workers):
+    """int32 words of each plan buffer, in PLAN_FIELDS order: the layout of the single plan
+    storage (sgld_plan_storage_words / sgld_plan_buffers_in_storage)."""
+    b = batch_capacity
+    e = b * max_splits
+    t = e * groups
+    return (b, b, 1, b, b + 1, b, e, e, e, e, e, e, t, t, 1, 1, 1, 1, workers, t, b * groups)
 
 
 class PlanBuffersC(ctypes.Structure):
@@ -55,8 +64,8 @@ DTYPE_F16, DTYPE_BF16, DTYPE_E4M3 = 0, 1, 2
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error"}
 EXPORTS = ("sgld_abi_version", "sgld_last_error", "sgld_layer_workspace_bytes", "sgld_plan_build",
            "sgld_decode_persistent", "sgld_merge_splits", "sgld_decode_persistent_noalloc",
-           "sgld_decode_kernel_kind")
-ABI_VERSION = 8
+           "sgld_decode_kernel_kind", "sgld_plan_storage_words", "sgld_plan_buffers_in_storage")
+ABI_VERSION = 9
 KERNEL_KINDS = {0: "mma.sync", 1: "tcgen05", 2: "tcgen05+tma", 3: "mma.sync+tma", 4: "small"}
 
 _lock = threading.Lock()
@@ -98,6 +107,11 @@ def load(path=None):
         lib.sgld_decode_persistent_noalloc.argtypes = lib.sgld_decode_persistent.argtypes
         lib.sgld_decode_kernel_kind.restype = ctypes.c_int
         lib.sgld_decode_kernel_kind.argtypes = lib.sgld_decode_persistent.argtypes[:3]
+        lib.sgld_plan_storage_words.restype = ctypes.c_size_t
+        lib.sgld_plan_storage_words.argtypes = [ctypes.POINTER(PlanGeometry)]
+        lib.sgld_plan_buffers_in_storage.restype = ctypes.c_int
+        lib.sgld_plan_buffers_in_storage.argtypes = [ctypes.c_void_p, ctypes.POINTER(PlanGeometry),
+                                                     ctypes.POINTER(PlanBuffersC)]
         lib.sgld_merge_splits.restype = ctypes.c_int
         lib.sgld_merge_splits.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int32] * 5 + [ctypes.c_void_p]
         if lib.sgld_abi_version() != ABI_VERSION:

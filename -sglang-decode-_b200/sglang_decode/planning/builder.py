@@ -10,7 +10,7 @@ from .. import _native
 
 def build_plan(plan, force_mode=-1):
     """Enqueue the plan build for ``plan`` (a PlanBuffers) on the current stream."""
-    _native.ops().plan_build(plan.tensors, plan.geometry, int(force_mode),
+    _native.ops().plan_build(plan.storage, plan.geometry, int(force_mode),
                              plan.rules if plan.rule_count else None, plan.rule_count, plan.counters)
 
 

@@ -46,6 +46,8 @@ class DecodeEngine:
         self.layers = [LayerBuffers.allocate(config, self.plan.device, dtype, counter=self.counters[i])
                        for i in range(layers)]
         self._calls = {}       # layer -> arguments of its last execute (for c_args)
+        self._default_scale = config.head_dim ** -0.5
+        self._decode = _native.ops().decode
 
     def prepare(self):
         """Call once per compatible group per step, including on every graph replay."""
@@ -73,71 +75,24 @@ class DecodeEngine:
           ``e4m3(x / k_scale)``, saturating) by a kernel chained right before the decode,
           so the result equals ``set_kv_buffer`` followed by the decode.
         """
-        c, p, out = self.config, self.plan, self.layers[layer]
-        kv_fp8 = k.dtype == _FP8
-        if q.dtype not in _DTYPES or v.dtype != k.dtype or (k.dtype != q.dtype and not kv_fp8):
-            raise ValueError("BF16/FP16 Q/K/V of identical dtype are required (or fp8 e4m3 K/V)")
-        if kv_fp8 and c.head_dim != 128:
-            raise ValueError("fp8 K/V are supported for head_dim 128")
-        if (q.ndim != 3 or tuple(q.shape[1:]) != (c.query_heads, c.head_dim)
-                or not 1 <= q.shape[0] <= c.batch_capacity):
-            raise ValueError("Q must be [rows <= capacity, query_heads, head_dim]")
-        if out.output.dtype != q.dtype:
-            raise ValueError("Q dtype differs from the engine's output dtype")
-        for t in (q, k, v, pages):
-            if t.device != p.device:
-                raise ValueError("all tensors must live on the engine's device")
-        if pages.dtype != torch.int32:
-            raise ValueError("page table / kv_indices must be int32")
-        if indptr is None:
-            if k.ndim != 4 or v.ndim != 4 or k.shape != v.shape:
-                raise ValueError("paged KV must have matching [page,token,head,dim] shapes")
-            if tuple(k.shape[1:]) != (c.page_size, c.kv_heads, c.head_dim):
-                raise ValueError("KV geometry differs from the capture configuration")
-            if tuple(pages.shape) != (c.batch_capacity, c.max_pages):
-                raise ValueError("page table capacity mismatch")
-            page_size = c.page_size
-        else:
-            if k.ndim != 3 or v.shape != k.shape or tuple(k.shape[1:]) != (c.kv_heads, c.head_dim):
-                raise ValueError("CSR KV must be [token,head,dim]")
-            if c.page_size != 1 or pages.ndim != 1:
-                raise ValueError("CSR integration uses one-token physical pages")
-            if indptr.dtype != torch.int32 or indptr.ndim != 1:
-                raise ValueError("kv_indptr must be a 1-D int32 tensor")
-            page_size = 1
-        k_scale, v_scale = float(k_scale), float(v_scale)
-        for name, value in (("k_scale", k_scale), ("v_scale", v_scale)):
-            if not value > 0.0 or value == float("inf"):
-                raise ValueError(f"{name} must be a finite value > 0")
-        scale = c.head_dim ** -0.5 if scale is None else float(scale)
-        cap = float(logit_cap or 0.0)
-        if not cap >= 0.0 or cap == float("inf"):
-            raise ValueError("logit_cap must be a finite value >= 0 (0 disables it)")
-        if new_loc is None:
-            if k_new is not None or v_new is not None:
-                raise ValueError("k_new / v_new need new_loc")
-        else:
-            rows = q.shape[0]
-            for t in (k_new, v_new):
-                if (t is None or t.dtype != q.dtype or t.device != p.device
-                        or tuple(t.shape) != (rows, c.kv_heads, c.head_dim)):
-                    raise ValueError("k_new / v_new must be [q rows, kv_heads, head_dim] in Q's dtype")
-            if (new_loc.dtype not in (torch.int64, torch.int32) or new_loc.device != p.device
-                    or new_loc.ndim != 1 or new_loc.shape[0] != rows or new_loc.stride(0) != 1):
-                raise ValueError("new_loc must be a contiguous 1-D int64/int32 tensor, one slot per Q row")
-        call = (q, k, v, pages, indptr, out.output, out.partial, out.lse, out.counter, out.status, p.tensors,
-                p.geometry, c.query_heads, c.kv_heads, c.head_dim, page_size, scale, cap, k_scale, v_scale,
-                k_new, v_new, new_loc)
+        out = self.layers[layer]
+        # Argument checks run in the operator (C++): wrong dtypes, shapes, devices or
+        # scales raise ValueError there, before anything is enqueued.
+        call = (q, k, v, pages, indptr, out.output, out.partial, out.lse, out.counter, out.status,
+                self.plan.storage, self.plan.geometry, self.config.page_size,
+                self._default_scale if scale is None else float(scale), float(logit_cap or 0.0),
+                float(k_scale), float(v_scale), k_new, v_new, new_loc)
         self._calls[layer] = call
-        _native.ops().decode(*call)          # torch.ops.sglang_decode.decode -> sgld_decode_persistent
+        self._decode(*call)          # torch.ops.sglang_decode.decode -> sgld_decode_persistent
         return out.output
 
     def c_args(self, layer=0):
         """The ``sgld_decode_args`` (ctypes) of this layer's last ``execute`` call, for callers
         that use the C ABI directly (e.g. ``sgld_decode_kernel_kind`` or the allocation-free
         entry point).  The struct points at the same tensors as that call."""
-        (q, k, v, pages, indptr, output, partial, lse, counter, status, _, _, hq, hkv, d, page_size, scale, cap,
-         k_scale, v_scale, k_new, v_new, new_loc) = self._calls[layer]
+        (q, k, v, pages, indptr, output, partial, lse, counter, status, _, _, page_size, scale, cap, k_scale, v_scale,
+         k_new, v_new, new_loc) = self._calls[layer]
+        hq, hkv, d = self.config.query_heads, self.config.kv_heads, self.config.head_dim
         a = _native.DecodeArgs()
         a.q, a.k, a.v, a.out, a.pages = q.data_ptr(), k.data_ptr(), v.data_ptr(), output.data_ptr(), pages.data_ptr()
         if indptr is None:

@@ -15,7 +15,8 @@ from ..config import DecodeConfig
 
 
 class PlanBuffers:
-    """Plan arrays, sized Bcap / E = Bcap*Smax / T = E*Hkv / W (workspace.py:7-23)."""
+    """Plan arrays, sized Bcap / E = Bcap*Smax / T = E*Hkv / W (workspace.py:7-23).  The same
+    attribute names as the reference; here they are views of one storage tensor."""
 
     def __init__(self, config: DecodeConfig, device, rules=()):
         self.config = config
@@ -23,25 +24,20 @@ class PlanBuffers:
         if self.device.type == "cuda" and self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
 
-        def ints(n):
-            return torch.zeros(n, dtype=torch.int32, device=self.device)
-
-        b, e, t = config.batch_capacity, config.record_capacity, config.task_capacity
-        self.lengths, self.splits = ints(b), ints(b)
-        self.active = ints(1)
-        self.counts, self.offsets, self.chunk = ints(b), ints(b + 1), ints(b)
-        self.request, self.split, self.begin, self.end, self.weight = [ints(e) for _ in range(5)]
-        self.order, self.pack_first, self.pack_count = ints(e), ints(t), ints(t)
-        self.record_count, self.num_packs, self.mode, self.error = [ints(1) for _ in range(4)]
-        self.static_head, self.static_next = ints(config.workers), ints(t)
+        # Every plan buffer is a view of one int32 storage, in sgld_plan_buffers order
+        # (sgld_plan_buffers_in_storage): the operators take the plan as that single tensor.
+        sizes = _native.plan_field_words(config.batch_capacity, config.max_splits, config.kv_heads, config.workers)
+        self.storage = torch.zeros(sum(sizes), dtype=torch.int32, device=self.device)
+        offset = 0
+        for name, n in zip(_native.PLAN_FIELDS, sizes):
+            setattr(self, name, self.storage[offset:offset + n])
+            offset += n
         rows = [[r.min_tasks, r.max_tasks, r.min_ratio, r.max_ratio, r.mode] for r in rules]
         self.rules = torch.tensor(rows or [[0, 0, 100, 100, 1]], dtype=torch.int32, device=self.device)
         self.rule_count = len(rows)
         self.has_static_rule = any(row[4] == 2 for row in rows)
         self.counters = None
-        # Operator views (torch.ops.sglang_decode): the buffers in sgld_plan_buffers order and
-        # the geometry (batch_capacity, max_splits, max_context, groups, workers).
-        self.tensors = [getattr(self, name) for name in _native.PLAN_FIELDS]
+        # Operator geometry (batch_capacity, max_splits, max_context, groups, workers).
         self.geometry = [config.batch_capacity, config.max_splits, config.max_context, config.kv_heads,
                          config.workers]
         # C views: pointers are stable for the lifetime of this object.

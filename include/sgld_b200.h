@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define SGLD_ABI_VERSION 8
+#define SGLD_ABI_VERSION 9
 
 typedef enum sgld_status {
   SGLD_OK = 0,
@@ -76,7 +76,19 @@ typedef struct sgld_plan_buffers {
   int32_t* error;        /* [1]   non-zero: invalid metadata            */
   int32_t* static_head;  /* [W]   STATIC list heads                     */
   int32_t* static_next;  /* [T]   STATIC list links                     */
+  int32_t* arrivals;     /* [B*groups] split arrivals per (request, KV head) of the small-batch
+                            kernel's fused merge: zeroed by every plan build and left zero by
+                            every decode (an addition: no reference counterpart)            */
 } sgld_plan_buffers;
+
+/*
+ * One int32 storage for every plan buffer: the number of int32 words it needs, and the
+ * sgld_plan_buffers that views it (buffers in declaration order, sizes as above).  Lets a caller
+ * allocate and pass the plan as a single array.  No counterpart in the reference (its
+ * PlanBuffers are separate tensors, runtime/workspace.py:7-23).
+ */
+size_t sgld_plan_storage_words(const sgld_plan_geometry* geometry);
+int sgld_plan_buffers_in_storage(int32_t* storage, const sgld_plan_geometry* geometry, sgld_plan_buffers* out);
 
 /*
  * Build the step's task table on the GPU (one launch, one CTA).

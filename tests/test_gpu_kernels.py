@@ -181,3 +181,47 @@ def test_small_kernel_is_bitwise_equal_to_the_persistent_kernel_on_single_stage_
         assert (engine.plan.end[:n] - engine.plan.begin[:n]).max().item() <= 64
         outs[kernel] = out.clone()
     assert torch.equal(outs["mma"], outs["small"])
+
+
+def test_small_kernel_fused_merge_edges(monkeypatch):
+    """The small-batch kernel merges the splits itself (the last split CTA of a request's KV
+    head merges its rows).  Zero-length and inactive requests give zero rows, the arrival
+    counters are left at zero so several layers run on one plan, invalid metadata turns every
+    row NaN, and an empty batch writes zeros -- the stand-alone merge kernel's rules."""
+    monkeypatch.setenv("SGLD_DECODE_KERNEL", "small")
+    lengths = [0, 65, 300, 0, 1000, 1]
+    c = DecodeConfig(batch_capacity=8, max_splits=8, max_context=1024, query_heads=16, kv_heads=2, head_dim=128,
+                     page_size=1, workers=37)
+    q, k, v, idx, indptr = (t.cuda() for t in make_csr_inputs(c, lengths, device="cpu", pool=2000))
+    expected = oracle_csr(q, k, v, indptr, idx, lengths)
+    engine = DecodeEngine(c, layers=3, force_mode=Mode.D1)
+    update_plan(engine, lengths)
+    engine.prepare()
+    for layer in range(3):
+        engine.layers[layer].output.fill_(float("nan"))
+        engine.layers[layer].partial.fill_(float("nan"))
+        engine.execute(q, k, v, idx, layer=layer, indptr=indptr)
+    torch.cuda.synchronize()
+    assert engine.kernel_kind() == "small"
+    assert engine.plan.arrivals.eq(0).all(), "arrival counters not left at zero"
+    for layer in range(3):
+        out = engine.layers[layer].output
+        assert engine.layers[layer].status.item() == 0
+        assert_within_tolerance(out, expected, len(lengths))
+        assert (out[len(lengths):].float() == 0).all(), "inactive rows must be zero"
+        assert (out[0].float() == 0).all() and (out[3].float() == 0).all(), "zero-length rows must be zero"
+
+    engine.plan.lengths[2] = c.max_context + 1                       # invalid metadata
+    engine.prepare()
+    out = engine.execute(q, k, v, idx, indptr=indptr)
+    torch.cuda.synchronize()
+    assert engine.plan.error.item() == 1
+    assert torch.isnan(out.float()).all()
+
+    update_plan(engine, [])                                          # empty batch
+    engine.layers[0].output.fill_(float("nan"))
+    engine.prepare()
+    out = engine.execute(q, k, v, idx, indptr=indptr)
+    torch.cuda.synchronize()
+    assert (out.float() == 0).all()
+    assert engine.plan.arrivals.eq(0).all()
