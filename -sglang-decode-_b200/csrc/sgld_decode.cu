@@ -205,54 +205,79 @@ struct Kernel {
 
   // R0 / R1 (static stride W): the tasks a CTA will claim are known in advance (worker,
   // worker + W, ...), so lanes 0..kLook-1 of the scheduler warp resolve the next kLook tasks
-  // in parallel (each a chain of dependent global loads: order, record fields, request
-  // counts / indptr) and lane 0 pushes them in claim order.  The serial claim loop costs
-  // those round trips once per task, which dominates small batches.
+  // in parallel (each a chain of dependent global loads: record fields, request counts /
+  // indptr) and lane 0 pushes them in claim order.  The serial claim loop costs those round
+  // trips once per task, which dominates small batches.
+  //
+  // R1's last rounds are claimed from the layer's claim counter instead of by stride: SMs
+  // stream at measurably different rates (on B200 the CTAs of a C3 step finished up to
+  // 110 us apart with equal task counts), so a fully static split leaves the fastest SMs
+  // idle for the tail.  The task set is R1's and each task runs once, so the outputs are
+  // bit-identical; R0, the prefix-search ablation, stays a pure stride.
   static constexpr int kLook = 4;
 
-  __device__ static void scheduler_strided(const DecodeLaunch& a, Misc& ms, int mode) {
+  // One task of an R0 / R1 plan (attention.py:23-47).  The caller checks the task against the
+  // task count: a task past it reads an in-bounds record and must be dropped.
+  __device__ static TaskDesc resolve_strided(const DecodeLaunch& a, int mode, int task) {
     const sgld_plan_buffers& p = a.p;
-    const int lane = threadIdx.x & 31;
     const int G = a.d.kv_heads;
+    TaskDesc t{};
+    t.valid = 0;
+    t.group = task % G;
+    const int record = min(task / G, a.bcap * a.smax - 1);   // in bounds while the count is in flight
+    if (mode == 0) {   // attention.py:25-39 -- upper-bound search over offsets
+      int lo = 0, hi = *p.active;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (record >= p.offsets[mid + 1]) lo = mid + 1;
+        else hi = mid;
+      }
+      t.request = lo;
+      t.split = record - p.offsets[lo];
+      const int chunk = p.chunk[lo];
+      t.begin = t.split * chunk;
+      t.end = min(t.begin + chunk, p.lengths[lo]);
+    } else {           // attention.py:41-47; an R1 plan's order is the identity (kernels/plan.py:72-74)
+      t.request = p.request[record];
+      t.split = p.split[record];
+      t.begin = p.begin[record];
+      t.end = p.end[record];
+    }
+    // never produced by a valid plan; skipping keeps every access in bounds
+    if (!(t.request < 0 || t.request >= a.bcap || t.end <= t.begin || t.split < 0 || t.split >= a.smax)) {
+      t.count_r = p.counts[t.request];
+      t.base = a.csr ? a.d.indptr[t.request] : t.request;
+      t.valid = 1;
+      if (a.fast_q && t.request < a.q_rows) prefetch_q(a, t);
+    }
+    return t;
+  }
+
+  __device__ static void scheduler_strided(const DecodeLaunch& a, Misc& ms, int mode) {
+    const int lane = threadIdx.x & 31;
     const int W = gridDim.x;
-    const int total = *p.record_count * G;
+    // The task count is only used after the first record loads are issued (their addresses
+    // do not depend on it), so its round trip overlaps theirs.
+    const int total = *a.p.record_count * a.d.kv_heads;
     int ti = 0;
     uint32_t tph = 0;
     bool ok = true;
-    for (int base = blockIdx.x; ok && base < total; base += kLook * W) {
+    int static_end = -1;
+    for (int base = blockIdx.x; ok; base += kLook * W) {
       const int task = base + lane * W;
       TaskDesc t{};
       t.valid = 0;
-      if (lane < kLook && task < total) {
-        t.group = task % G;
-        int record = task / G;
-        if (mode == 0) {   // attention.py:25-39 -- upper-bound search over offsets
-          int lo = 0, hi = *p.active;
-          while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (record >= p.offsets[mid + 1]) lo = mid + 1;
-            else hi = mid;
-          }
-          t.request = lo;
-          t.split = record - p.offsets[lo];
-          const int chunk = p.chunk[lo];
-          t.begin = t.split * chunk;
-          t.end = min(t.begin + chunk, p.lengths[lo]);
-        } else {           // attention.py:41-47
-          record = p.order[record];
-          t.request = p.request[record];
-          t.split = p.split[record];
-          t.begin = p.begin[record];
-          t.end = p.end[record];
-        }
-        // never produced by a valid plan; skipping keeps every access in bounds
-        if (!(t.request < 0 || t.request >= a.bcap || t.end <= t.begin || t.split < 0 || t.split >= a.smax)) {
-          t.count_r = p.counts[t.request];
-          t.base = a.csr ? a.d.indptr[t.request] : t.request;
-          t.valid = 1;
-          if (a.fast_q && t.request < a.q_rows) prefetch_q(a, t);
+      if (lane < kLook) t = resolve_strided(a, mode, task);
+      if (static_end < 0) {
+        // Static rounds (every round for R0); R1 leaves about an eighth of them, at least
+        // two, to the claimed tail.
+        static_end = total;
+        if (mode == 1) {
+          const int rounds = total / W;
+          static_end = (rounds - min(rounds, max(2, rounds / 8))) * W;
         }
       }
+      if (task >= static_end) t.valid = 0;
       for (int l = 0; l < kLook; ++l) {
         TaskDesc u;
         u.request = __shfl_sync(0xffffffffu, t.request, l);
@@ -267,8 +292,16 @@ struct Kernel {
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
       }
+      if (base + kLook * W >= static_end) break;
     }
+    // R1 tail: tasks [static_end, total) one claim at a time.
     if (lane == 0) {
+      while (ok && static_end < total) {
+        const int task = static_end + atomicAdd(a.d.counter, 1);
+        if (task >= total) break;
+        const TaskDesc t = resolve_strided(a, mode, task);
+        if (t.valid) ok = push_task(ms, ti, tph, t, a.d.status);
+      }
       TaskDesc end_marker{};
       end_marker.valid = 0;
       push_task(ms, ti, tph, end_marker, a.d.status);
@@ -283,6 +316,9 @@ struct Kernel {
     const int mode = *p.mode;
     const int total = *p.record_count * G;
     const bool dynamic = mode >= 3;
+    // D1 packs are single tasks in pack order: with width 1 the plan writes pack_first[c] = c
+    // and pack_count[c] = 1 (kernels/plan.py:84-99), so a D1 claim is the task itself.
+    const bool d1 = mode == 3;
     int ti = 0;
     uint32_t tph = 0;
     int cursor, limit;
@@ -300,7 +336,7 @@ struct Kernel {
     bool ok = true;
     while (ok && cursor >= 0 && cursor < limit) {
       int first = cursor, count = 1;
-      if (dynamic) {
+      if (dynamic && !d1) {
         first = p.pack_first[cursor];
         count = p.pack_count[cursor];
       }
@@ -321,8 +357,8 @@ struct Kernel {
           const int chunk = p.chunk[lo];
           t.begin = t.split * chunk;
           t.end = min(t.begin + chunk, p.lengths[lo]);
-        } else {           // attention.py:41-47
-          if (mode != 2) record = p.order[record];
+        } else {           // attention.py:41-47; an R1 plan's order is the identity (kernels/plan.py:72-74)
+          if (mode >= 3) record = p.order[record];
           t.request = p.request[record];
           t.split = p.split[record];
           t.begin = p.begin[record];

@@ -6,7 +6,7 @@
 // split slots, in split order (m' = max(m, l_s), acc = acc*e^(m-m') + p_s*e^(l_s-m'), same
 // for the denominator), result acc / max(den, 1e-30).  The multiply-adds are written as
 // explicit __fmaf_rn / __fmul_rn so that the compiler cannot contract them differently at
-// the two call sites.  Loads are issued eight splits at a time (a few memory round trips per
+// the two call sites.  Loads are issued kUnroll splits at a time (a few memory round trips per
 // row, not one per split) and bypass L1 (.cg): the slots were written by other CTAs.
 #pragma once
 
@@ -18,10 +18,11 @@ namespace sgld {
 
 constexpr float kMergeLog2e = 1.4426950408889634f;
 
-// `lse_row` = lse + row * smax, `partial_row` = partial + row * smax * d_dim + d.
+// `lse_row` = lse + row * smax, `partial_row` = partial + row * smax * d_dim + d.  kUnroll
+// splits are loaded at a time; it changes the load batching only, not the arithmetic order.
+template <int kUnroll = 8>
 __device__ __forceinline__ float4 merge_row4(const float* __restrict__ partial_row, const float* __restrict__ lse_row,
                                              int n, int d_dim) {
-  constexpr int kUnroll = 8;
   float mm = -INFINITY, den = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int s0 = 0; s0 < n; s0 += kUnroll) {

@@ -452,9 +452,12 @@ __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
   for (int i = 0; i < rows_per_thread; ++i) {
     const int r = tid * rows_per_thread + i;
     if (r >= bcap) break;
+    // Loaded whatever `active` is (every row of the capacity is allocated), so these loads
+    // and the load of `active` share one round trip.
+    const int len_in = p.lengths[r], spl_in = p.splits[r];
     const bool live = r < active;
-    const int len = live ? p.lengths[r] : 0;
-    const int spl = live ? p.splits[r] : 1;
+    const int len = live ? len_in : 0;
+    const int spl = live ? spl_in : 1;
     const bool invalid = live && (len < 0 || len > a.maxctx || spl < 1 || spl > a.smax);
     invalid_any |= invalid ? 1 : 0;
     const int chunk = wrap32(static_cast<long long>(cdiv32(cdiv32(max(len, 0), max(spl, 1)), kSplitAlign)) * kSplitAlign);
