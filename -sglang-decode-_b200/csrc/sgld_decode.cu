@@ -294,13 +294,25 @@ struct Kernel {
       }
       if (base + kLook * W >= static_end) break;
     }
-    // R1 tail: tasks [static_end, total) one claim at a time.
+    // R1 tail: tasks [static_end, total) one claim at a time, each claimed only once the
+    // indexer has taken the task pushed before it, so a CTA holds few claimed tasks and the
+    // CTAs finish close together.
     if (lane == 0) {
+      int last_slot = -1;
+      uint32_t last_phase = 0;
       while (ok && static_end < total) {
+        if (last_slot >= 0 && !mbar_wait(&ms.tempty[last_slot], last_phase, global_timer_ns() + kWaitLimitNs)) {
+          atomicOr(a.d.status, kStatusWaitTask);
+          ok = false;
+          break;
+        }
         const int task = static_end + atomicAdd(a.d.counter, 1);
         if (task >= total) break;
         const TaskDesc t = resolve_strided(a, mode, task);
-        if (t.valid) ok = push_task(ms, ti, tph, t, a.d.status);
+        if (!t.valid) continue;
+        last_slot = ti;
+        last_phase = tph;
+        ok = push_task(ms, ti, tph, t, a.d.status);
       }
       TaskDesc end_marker{};
       end_marker.valid = 0;
