@@ -42,6 +42,7 @@ for _p in (str(ROOT), str(ROOT / "-sglang-decode-_b200")):
 
 FALLBACK_HBM_GBS = 6650.0
 REF_ROUNDS = 3          # parallel CPU rounds per reference-arm step
+L2_BYTES = 126 * 2**20  # B200 L2
 METRIC = "paged GQA decode µs/layer + achieved HBM TB/s vs peak at 1/2/4/8 B200"
 
 
@@ -419,26 +420,53 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
 
-    # ---- device-timed region (inputs resident in HBM; KV pool >> L2, no flush needed).  The
-    # step loop records no event between its launches: an event between two kernels would
-    # cut the programmatic dependent launches that chain plan -> decode -> merge -> next plan.
+    # ---- device-timed region (inputs resident in HBM).  With a KV pool far larger than the
+    # 126 MB L2 no flush is needed, and the step loop records no event between its launches:
+    # an event between two kernels would cut the programmatic dependent launches that chain
+    # plan -> decode -> merge -> next plan.  A pool that (nearly) fits in L2 (C1: 64 MB) would
+    # stay cached from one step to the next, so then every timed step is preceded by a write
+    # of twice the L2 size and timed alone between its own events.
     stream = torch.cuda.current_stream(device)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kv_bytes = k.numel() * k.element_size() + v.numel() * v.element_size()
+    flush = kv_bytes < 4 * L2_BYTES
+    scrub = torch.empty(2 * L2_BYTES // 4, dtype=torch.int32, device=device) if flush else None
+
+    def timed_steps(n, body, before=None):
+        """Device ms of n calls of body(): one event pair around the loop, or with the L2
+        flush, the sum of per-call event pairs with the flush (and `before`) outside them."""
+        if not flush:
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(n):
+                if before is not None:
+                    before()
+                body()
+            s1.record(stream)
+            torch.cuda.synchronize()
+            return s0.elapsed_time(s1)
+        pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for e0, e1 in pairs:
+            scrub.zero_()
+            if before is not None:
+                before()
+            e0.record(stream)
+            body()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return sum(e0.elapsed_time(e1) for e0, e1 in pairs)
+
     with ClockSampler(local) as clocks:
         barrier()
         torch.cuda.synchronize()
-        start.record(stream)
-        for _ in range(args.steps):
-            step()
-        end.record(stream)
-        torch.cuda.synchronize()
+        total_ms = timed_steps(args.steps, step)
         barrier()
-        total_ms = start.elapsed_time(end)
         # Kernel-only time for the roofline: the same steps with events around the decode +
         # merge launches (or the whole step with the KV-cache write).
         dec_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                       for _ in range(args.steps)]
         for i in range(args.steps):
+            if flush:
+                scrub.zero_()
             if kv_write != "none":
                 dec_events[i][0].record(stream)
                 step()
@@ -471,13 +499,7 @@ def run_ours(args):
         for _ in range(3):
             graph.replay()
         torch.cuda.synchronize()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        g1.record(stream)
-        torch.cuda.synchronize()
-        graph_us = g0.elapsed_time(g1) * 1000 / args.steps
+        graph_us = timed_steps(args.steps, graph.replay) * 1000 / args.steps
         del graph
 
     # ---- end to end through the public API: every step copies its inputs (q, lengths/splits,
@@ -518,6 +540,8 @@ def run_ours(args):
 
     def compute(i):
         sl, buf = i % 2, bufs[i % 2]
+        if flush:
+            scrub.zero_()          # its time is subtracted below
         stream.wait_event(uploaded[sl])
         if i >= 2:
             stream.wait_event(downloaded[sl])
@@ -551,6 +575,14 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if flush:                      # take out the per-step L2 scrub, timed on its own
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(20):
+            scrub.zero_()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms -= f0.elapsed_time(f1) / 20
     if not torch.equal(h_out[(e2e_steps - 1) % 2][:n_req], out_check[:n_req].cpu()):
         raise SystemExit("e2e output differs from the device-resident run")
 
@@ -591,7 +623,11 @@ def run_ours(args):
                        "mode_run": int(engine.plan.mode.item()),
                        "policy": Path(args.policy).name if args.policy else None,
                        "heads_per_gpu": {"kv": hkv, "q": hq}, "workers": sms,
-                       "l2": "not flushed: KV pool per GPU > 126 MB L2", "kv_write": kv_write,
+                       "l2": (f"flushed: a {2 * L2_BYTES >> 20} MB write before every timed step (KV pool "
+                              f"{kv_bytes >> 20} MB < 4 x 126 MB L2), steps timed one by one; e2e minus the "
+                              f"measured write" if flush else
+                              f"not flushed: KV pool per GPU {kv_bytes >> 20} MB > 4 x 126 MB L2"),
+                       "kv_write": kv_write,
                        "self_check": "status 0, finite, sampled requests within 2e-2/2e-3 of FP32",
                        "decode_kernel": kind,
                        "graph_step_us": round(graph_us, 2) if graph_us is not None else None},
