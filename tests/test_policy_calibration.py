@@ -102,6 +102,7 @@ def test_shipped_b200_policy_is_validated_by_its_evidence():
     for ev in art["evidence"]:
         assert hashlib.sha256((root / ev["path"]).read_bytes()).hexdigest() == ev["sha256"]
     rules = load_policy(root / "b200_skewed.json")
-    assert [r.mode for r in rules] == [3]                 # D1 for skewed batches on B200
+    # With R1's claimed tail, D1 no longer clears the 3% gate on the C2 skew: R1 is published.
+    assert [r.mode for r in rules] == [1]
     cal, hold = (C.read_rows(root / ev["path"]) for ev in art["evidence"])
-    assert C.choose(cal, hold) == "D1"                    # the gates reproduce the published choice
+    assert C.choose(cal, hold) == "R1"                    # the gates reproduce the published choice
