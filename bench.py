@@ -436,6 +436,9 @@ def run_ours(args):
         flush, the sum of per-call event pairs with the flush (and `before`) outside them."""
         if not flush:
             s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            # A ~1 ms spin ahead of the start event lets the host queue the first steps before
+            # the GPU reaches them, so a short run does not time the host's first launches.
+            torch.cuda._sleep(2_000_000)
             s0.record(stream)
             for _ in range(n):
                 if before is not None:
@@ -594,6 +597,7 @@ def run_ours(args):
         gathered = [torch.zeros_like(stats) for _ in range(world)]
         dist.all_gather(gathered, stats)
         per_rank = [round(g[1].item() * 1000, 2) for g in gathered]
+        per_rank_step = [round(g[0].item() * 1000, 2) for g in gathered]
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     step_ms, dec_ms, e2e_ms = stats.tolist()
     bytes_launch = algorithmic_bytes(b, hkv, hq, kv_elem=1 if fp8 else None)
@@ -645,6 +649,7 @@ def run_ours(args):
         }
         if per_rank is not None:
             line["per_rank_kernel_us"] = per_rank
+            line["per_rank_step_us"] = per_rank_step
         if args.shard:
             line["config"]["shard"] = args.shard
         if cpu is not None:
