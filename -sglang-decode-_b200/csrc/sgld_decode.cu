@@ -61,11 +61,11 @@ enum : int { kStatusWaitFull = 1, kStatusWaitEmpty = 2, kStatusWaitQ = 4, kStatu
              kStatusStaticCycle = 16, kStatusWaitDesc = 32, kStatusQRows = 64 };
 
 struct StageHdr {
-  int request, split, group, ntok, flags, count_r, t0, pad;
+  int request, split, group, ntok, flags, t0, pad[2];
 };
 
 struct TaskDesc {
-  int request, split, group, begin, end, count_r, base, valid;
+  int request, split, group, begin, end, base, valid, pad;
 };
 
 template <int D, int NT, bool F8 = false>
@@ -245,7 +245,6 @@ struct Kernel {
     }
     // never produced by a valid plan; skipping keeps every access in bounds
     if (!(t.request < 0 || t.request >= a.bcap || t.end <= t.begin || t.split < 0 || t.split >= a.smax)) {
-      t.count_r = p.counts[t.request];
       t.base = a.csr ? a.d.indptr[t.request] : t.request;
       t.valid = 1;
       if (a.fast_q && t.request < a.q_rows) prefetch_q(a, t);
@@ -285,7 +284,6 @@ struct Kernel {
         u.group = __shfl_sync(0xffffffffu, t.group, l);
         u.begin = __shfl_sync(0xffffffffu, t.begin, l);
         u.end = __shfl_sync(0xffffffffu, t.end, l);
-        u.count_r = __shfl_sync(0xffffffffu, t.count_r, l);
         u.base = __shfl_sync(0xffffffffu, t.base, l);
         u.valid = __shfl_sync(0xffffffffu, t.valid, l);
         if (u.valid && lane == 0) ok = push_task(ms, ti, tph, u, a.d.status);
@@ -379,7 +377,6 @@ struct Kernel {
         if (t.request < 0 || t.request >= a.bcap || t.end <= t.begin || t.split < 0 ||
             t.split >= a.smax)
           continue;   // never produced by a valid plan; skipping keeps every access in bounds
-        t.count_r = p.counts[t.request];
         t.base = a.csr ? a.d.indptr[t.request] : t.request;
         t.valid = 1;
         // The task's query rows are read by producer 0 a few stages before the consumers
@@ -502,9 +499,8 @@ struct Kernel {
           h.group = b.t.group;
           h.ntok = min(C::kTS, b.t.end - t0);
           h.flags = (t0 == b.t.begin ? kFlagFirst : 0) | (t0 + C::kTS >= b.t.end ? kFlagLast : 0);
-          h.count_r = b.t.count_r;
           h.t0 = t0;
-          h.pad = 0;
+          h.pad[0] = h.pad[1] = 0;
           ms.shdr[sd] = h;
         }
         __syncwarp();
