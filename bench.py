@@ -18,7 +18,12 @@ the public API with per-step host->device copies of the step's inputs from pinne
 memory and a device->host copy of the output, on copy streams that overlap the
 neighbouring steps' compute), ``cpu_baseline`` (the FP32 CPU oracle on a bounded
 sample, scaled to one layer) and SM clocks sampled during the timed region.  Before
-timing, sampled requests are checked against a plain torch FP32 attention.
+timing, sampled requests are checked against a plain torch FP32 attention.  The steps are
+queued behind a short GPU spin and timed with one event pair (no event between launches, so
+the programmatic dependent launches stay chained); when the KV pool nearly fits in L2 (C1),
+L2 is flushed before every step and the steps are timed one by one instead.  The same step
+replayed from a CUDA graph is reported as ``config.graph_step_us``; small batches run the
+small-batch kernel with the merge fused in (``config.decode_kernel``).
 ``--impl reference`` times the reference's CPU implementation (the oracle restatement)
 instead; ``--shard R/N`` times rank R of an N-way head-sharded run on one GPU.
 """
