@@ -1002,7 +1002,8 @@ struct Kernel {
         v.w += r.w * sw[w];
       }
       const float vs = a.d.v_scale;
-      const float4 res = make_float4(v.x / gl * vs, v.y / gl * vs, v.z / gl * vs, v.w / gl * vs);
+      const float f = vs / gl;   // one division per item, not one per dim (IEEE division is a long sequence)
+      const float4 res = make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
       const int64_t slot = slot0 + static_cast<int64_t>(head) * smax;
       *reinterpret_cast<float4*>(a.d.partial + slot * D + d) = res;   // 16-byte aligned (checked at entry)
       if (d == 0) a.d.lse[slot] = (gm + lg2(gl)) * kLn2;
@@ -1350,7 +1351,8 @@ struct Small {
         v.w += r.w * sw[w];
       }
       const float vs = a.d.v_scale;
-      const float4 res = make_float4(v.x / gl * vs, v.y / gl * vs, v.z / gl * vs, v.w / gl * vs);
+      const float f = vs / gl;   // one division per item, not one per dim (IEEE division is a long sequence)
+      const float4 res = make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
       const int64_t slot = slot0 + static_cast<int64_t>(head) * a.smax;
       *reinterpret_cast<float4*>(a.d.partial + slot * D + d) = res;
       if (d == 0) a.d.lse[slot] = (gm + lg2(gl)) * kLn2;
