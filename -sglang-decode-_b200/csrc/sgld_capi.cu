@@ -167,7 +167,7 @@ size_t sgld_layer_workspace_bytes(int32_t batch_capacity, int32_t query_heads, i
   if (batch_capacity <= 0 || query_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || max_splits <= 0)
     return 0;
   const size_t slots = static_cast<size_t>(batch_capacity) * query_heads * max_splits;
-  return 2 * sizeof(int32_t)                                   /* counter + exit ticket */
+  return 2 * sizeof(int32_t)                                   /* claim counter + spare */
          + slots * head_dim * sizeof(float)                    /* partial */
          + slots * sizeof(float)                               /* lse */
          + sizeof(int32_t);                                    /* status */
@@ -440,7 +440,7 @@ int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers
   if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent launch");
   if (kind == SGLD_KERNEL_SMALL) return SGLD_OK;   // the small-batch kernel merges the splits itself
   e = sgld::launch_merge(d.partial, d.lse, plan->counts, plan->error, d.out, d.dtype, geometry->batch_capacity,
-                         d.query_heads, d.head_dim, geometry->max_splits, st, true);
+                         d.query_heads, d.head_dim, geometry->max_splits, st, true, d.counter);
   if (e != cudaSuccess) return cuda_fail(e, "sgld_decode_persistent merge launch");
   return SGLD_OK;
 }
@@ -459,7 +459,7 @@ int sgld_merge_splits(const float* partial, const float* lse, const int32_t* cou
     return fail(SGLD_ERR_UNSUPPORTED, "head_dim must be a multiple of 4 up to 4096");
   if (!aligned16(partial)) return fail(SGLD_ERR_INVALID_ARGUMENT, "partial must be 16-byte aligned");
   cudaError_t e = sgld::launch_merge(partial, lse, counts, error, out, dtype, batch_capacity, query_heads,
-                                     head_dim, max_splits, static_cast<cudaStream_t>(stream), false);
+                                     head_dim, max_splits, static_cast<cudaStream_t>(stream), false, nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "sgld_merge_splits launch");
   return SGLD_OK;
 }

@@ -35,8 +35,8 @@
 // chunk index XOR row%8) that TMA writes natively; ldmatrix reads are bank-conflict
 // free.  Rows past a task's last token are masked in registers (scores -inf, V
 // fragments zero), so stale shared memory never reaches the result.  Every mbarrier
-// wait is bounded; on expiry a status bit is set and the warp unwinds.  The claim
-// counter is left at zero.
+// wait is bounded; on expiry a status bit is set and the warp unwinds.  The merge
+// launched after this kernel leaves the claim counter at zero.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -243,6 +243,11 @@ struct Kernel {
       t.begin = p.begin[record];
       t.end = p.end[record];
     }
+    return finish_task(a, t);
+  }
+
+  // Validity check, CSR base and Q prefetch of a resolved task.
+  __device__ static TaskDesc finish_task(const DecodeLaunch& a, TaskDesc t) {
     // never produced by a valid plan; skipping keeps every access in bounds
     if (!(t.request < 0 || t.request >= a.bcap || t.end <= t.begin || t.split < 0 || t.split >= a.smax)) {
       t.base = a.csr ? a.d.indptr[t.request] : t.request;
@@ -252,12 +257,31 @@ struct Kernel {
     return t;
   }
 
-  __device__ static void scheduler_strided(const DecodeLaunch& a, Misc& ms, int mode) {
+  // The R1 record fields of this lane's first task (lanes 0..kLook-1), loaded before the
+  // mode is known: the addresses do not depend on it and every record slot is in bounds,
+  // so the loads share the mode's round trip.  Unused unless the mode is R1.
+  struct FirstRound {
+    int request, split, begin, end, records;
+  };
+  __device__ static FirstRound load_first_round(const DecodeLaunch& a) {
+    const int lane = threadIdx.x & 31;
+    const int task = blockIdx.x + lane * gridDim.x;
+    const int record = min(task / a.d.kv_heads, a.bcap * a.smax - 1);
+    FirstRound f{0, 0, 0, 0, 0};
+    if (lane < kLook) {
+      f.request = a.p.request[record];
+      f.split = a.p.split[record];
+      f.begin = a.p.begin[record];
+      f.end = a.p.end[record];
+    }
+    f.records = *a.p.record_count;
+    return f;
+  }
+
+  __device__ static void scheduler_strided(const DecodeLaunch& a, Misc& ms, int mode, const FirstRound& first) {
     const int lane = threadIdx.x & 31;
     const int W = gridDim.x;
-    // The task count is only used after the first record loads are issued (their addresses
-    // do not depend on it), so its round trip overlaps theirs.
-    const int total = *a.p.record_count * a.d.kv_heads;
+    const int total = first.records * a.d.kv_heads;
     int ti = 0;
     uint32_t tph = 0;
     bool ok = true;
@@ -266,7 +290,20 @@ struct Kernel {
       const int task = base + lane * W;
       TaskDesc t{};
       t.valid = 0;
-      if (lane < kLook) t = resolve_strided(a, mode, task);
+      if (lane < kLook) {
+        if (mode == 1 && base == static_cast<int>(blockIdx.x)) {
+          TaskDesc r{};
+          r.valid = 0;
+          r.group = task % a.d.kv_heads;
+          r.request = first.request;
+          r.split = first.split;
+          r.begin = first.begin;
+          r.end = first.end;
+          t = finish_task(a, r);
+        } else {
+          t = resolve_strided(a, mode, task);
+        }
+      }
       if (static_end < 0) {
         // Static rounds (every round for R0); R1 leaves about an eighth of them, at least
         // two, to the claimed tail.
@@ -1056,9 +1093,10 @@ struct Kernel {
     } else if (warp == C::kIndexerWarp) {
       indexer(a, smem, ms);
     } else {
+      const FirstRound first = load_first_round(a);
       const int mode = *a.p.mode;
       if (mode <= 1) {
-        scheduler_strided(a, ms, mode);
+        scheduler_strided(a, ms, mode, first);
       } else {
         if (lane == 0) scheduler(a, ms);
         __syncwarp();
@@ -1066,17 +1104,10 @@ struct Kernel {
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    // Let the dependent merge launch start filling SMs as this CTA leaves.
+    // Let the dependent merge launch start filling SMs as this CTA leaves.  The merge
+    // zeroes the claim words once this grid has completed, so the last CTA leaves without
+    // a fence-and-atomic exit chain on the step's critical path.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    // Exit ticket: the last CTA to finish leaves the claim counter at zero.
-    if (threadIdx.x == 0) {
-      __threadfence();
-      const int ticket = atomicAdd(a.d.counter + 1, 1);
-      if (ticket == static_cast<int>(gridDim.x) - 1) {
-        atomicExch(a.d.counter, 0);
-        atomicExch(a.d.counter + 1, 0);
-      }
-    }
   }
 };
 

@@ -961,15 +961,8 @@ struct TcKernel {
     __syncthreads();
     tc_fence_after();
     if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+    // The merge launched after this kernel zeroes the claim words once this grid completes.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (threadIdx.x == 0) {   // exit ticket: the last CTA leaves the claim counter at zero
-      __threadfence();
-      const int ticket = atomicAdd(a.d.counter + 1, 1);
-      if (ticket == static_cast<int>(gridDim.x) - 1) {
-        atomicExch(a.d.counter, 0);
-        atomicExch(a.d.counter + 1, 0);
-      }
-    }
   }
 };
 

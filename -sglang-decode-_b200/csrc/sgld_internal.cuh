@@ -86,8 +86,11 @@ int validate_decode(const sgld_decode_args* args, const sgld_plan_buffers* plan,
 void* current_context();
 
 // programmatic: launch as a programmatic dependent of the preceding kernel (PDL).
+// claim: the preceding decode's two claim words, zeroed once that decode has completed
+// (nullptr for a merge on its own).
 cudaError_t launch_merge(const float* partial, const float* lse, const int32_t* counts,
                          const int32_t* error, void* out, int32_t dtype, int32_t bcap, int32_t hq,
-                         int32_t d, int32_t smax, cudaStream_t stream, bool programmatic);
+                         int32_t d, int32_t smax, cudaStream_t stream, bool programmatic,
+                         int32_t* claim);
 
 }  // namespace sgld

@@ -32,8 +32,12 @@ __device__ __forceinline__ void store4(T* dst, float4 v) {
 template <typename T>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32) merge_kernel(
     const float* __restrict__ partial, const float* __restrict__ lse, const int32_t* __restrict__ counts,
-    const int32_t* __restrict__ error, T* __restrict__ out, int bcap, int hq, int d_dim, int smax) {
+    const int32_t* __restrict__ error, T* __restrict__ out, int bcap, int hq, int d_dim, int smax,
+    int32_t* __restrict__ claim) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The decode grid has completed: leave its two claim words at zero for the next decode
+  // on this layer (the decode kernel itself ends without touching them again).
+  if (claim != nullptr && blockIdx.x == 0 && threadIdx.x < 2) claim[threadIdx.x] = 0;
   const int row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);   // (request, head)
   const int lane = threadIdx.x & 31;
   if (row >= bcap * hq) return;
@@ -56,7 +60,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) merge_kernel(
 
 cudaError_t launch_merge(const float* partial, const float* lse, const int32_t* counts,
                          const int32_t* error, void* out, int32_t dtype, int32_t bcap, int32_t hq,
-                         int32_t d, int32_t smax, cudaStream_t stream, bool programmatic) {
+                         int32_t d, int32_t smax, cudaStream_t stream, bool programmatic, int32_t* claim) {
   cudaLaunchConfig_t cfg = {};
   const int64_t rows = static_cast<int64_t>(bcap) * hq;
   cfg.gridDim = dim3(static_cast<unsigned>((rows + kWarpsPerBlock - 1) / kWarpsPerBlock));
@@ -71,11 +75,11 @@ cudaError_t launch_merge(const float* partial, const float* lse, const int32_t* 
   if (dtype == SGLD_DTYPE_BF16) {
     return cudaLaunchKernelEx(&cfg, merge_kernel<__nv_bfloat16>, partial, lse, counts, error,
                               static_cast<__nv_bfloat16*>(out), static_cast<int>(bcap), static_cast<int>(hq),
-                              static_cast<int>(d), static_cast<int>(smax));
+                              static_cast<int>(d), static_cast<int>(smax), claim);
   }
   return cudaLaunchKernelEx(&cfg, merge_kernel<__half>, partial, lse, counts, error, static_cast<__half*>(out),
                             static_cast<int>(bcap), static_cast<int>(hq), static_cast<int>(d),
-                            static_cast<int>(smax));
+                            static_cast<int>(smax), claim);
 }
 
 }  // namespace sgld

@@ -5,8 +5,8 @@
 // provide per-layer scratch: plugin interfaces whose signature carries no workspace, or
 // servers that give all free device memory to their KV-cache pool at start-up and allow
 // no allocation afterwards (cudaMalloc also synchronises the device, which a serving
-// loop cannot afford).  For them the scratch of the decode -- the claim counter and exit
-// ticket, and the fp32 partial outputs and LSEs of every split slot -- lives in one
+// loop cannot afford).  For them the scratch of the decode -- the two claim words, and
+// the fp32 partial outputs and LSEs of every split slot -- lives in one
 // file-scope device array of kScratchBytes bytes, reserved on every GPU that loads the
 // library until the process exits.  The status word stays with the caller (a word inside
 // the array could not be read back, and a timed-out call would look like a good one).
@@ -18,7 +18,7 @@
 // stream capture.  The entry point allocates and frees nothing.
 //
 // Every call shares the one array and leaves its last contents there.  Each call clears
-// the words that must start at zero (claim counter, exit ticket) on its stream before the
+// the words that must start at zero (the two claim words) on its stream before the
 // decode, after every argument check has passed; calls whose GPU work overlaps
 // (different streams, or several threads) race on the array and must be serialised by
 // the caller.
@@ -61,7 +61,7 @@ extern "C" int sgld_decode_persistent_noalloc(const sgld_decode_args* args, cons
   if (geometry->batch_capacity <= 0 || geometry->max_splits <= 0 || args->query_heads <= 0 ||
       args->head_dim <= 0)
     return sgld::set_last_error(SGLD_ERR_INVALID_ARGUMENT, "geometry fields must be positive");
-  // Layout of the array: [256-byte header: counter, exit ticket][partial, rounded up to
+  // Layout of the array: [256-byte header: the two claim words][partial, rounded up to
   // 256 bytes][lse, rounded up to 256 bytes].
   const size_t slots = static_cast<size_t>(geometry->batch_capacity) * args->query_heads * geometry->max_splits;
   const size_t partial_bytes = round_up(slots * args->head_dim * sizeof(float), 256);
@@ -101,7 +101,7 @@ extern "C" int sgld_decode_persistent_noalloc(const sgld_decode_args* args, cons
   const int rc = sgld::validate_decode(&a, plan, geometry);
   if (rc != SGLD_OK) return rc;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The claim counter and exit ticket must start at zero; everything else is written
+  // The two claim words must start at zero; everything else is written
   // before it is read.
   if (cudaMemsetAsync(base, 0, 2 * sizeof(int32_t), st) != cudaSuccess)
     return sgld::set_last_error(SGLD_ERR_CUDA, "clearing the no-alloc scratch header failed");

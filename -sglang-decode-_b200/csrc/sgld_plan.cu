@@ -21,6 +21,7 @@
 #include <mutex>
 
 #include "sgld_internal.cuh"
+#include "sgld_ptx.cuh"
 
 namespace sgld {
 namespace {
@@ -436,6 +437,19 @@ __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const sgld_plan_buffers& p = a.p;
   const int bcap = a.bcap, G = a.groups, W = a.workers;
+  // The inputs read first (active count, lengths, split hints) are plan buffers of the
+  // geometry's size, written before this launch.  Warming their sectors in L2 while the
+  // preceding kernel drains takes an HBM round trip off those loads; a prefetch is only a
+  // hint, and the loads after the wait below read the current values.
+  {
+    const int sectors = (bcap + 7) >> 3;             // 8 int32 per 32-byte sector
+    for (int j = tid; j <= 2 * sectors; j += kThreads) {
+      const int32_t* src = j == 2 * sectors ? p.active
+                           : j < sectors    ? p.lengths + min(j * 8, bcap - 1)
+                                            : p.splits + min((j - sectors) * 8, bcap - 1);
+      prefetch_l2(src);
+    }
+  }
   // Launched as a programmatic dependent of the preceding kernel (the previous step's
   // merge, which still reads counts / error): the block is resident early, and waits here
   // for that kernel's completion before reading its inputs or writing any plan buffer.
@@ -524,7 +538,6 @@ __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
     p.end[i] = e;
     p.weight[i] = w;
     s.weight[i] = w;
-    if (w <= kMaxTableWeight) atomicAdd(&s.hist[w], 1);
     vmax = max(vmax, w);
     vmin = min(vmin, w);
   }
@@ -620,7 +633,13 @@ __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
 
   // ---------------------------------------------------------------- 4. STATIC LPT lists
   if (W > kThreads) static_lists_serial(a, s, total, G, W);
-  else if (max_w <= kMaxTableWeight) static_lists_runs(a, s, blk, s.skey32, total, G, W, true);
+  else if (max_w <= kMaxTableWeight) {
+    // The weight histogram (run weights of the table path) is only needed here, so it is
+    // counted here rather than during emission, which every mode runs.
+    for (int i = tid; i < total; i += kThreads) atomicAdd(&s.hist[s.weight[i]], 1);
+    __syncthreads();
+    static_lists_runs(a, s, blk, s.skey32, total, G, W, true);
+  }
   else static_lists_runs(a, s, blk, s.skey64, total, G, W, false);
 }
 

@@ -106,6 +106,11 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
 }
 
 // Bring `bytes` at `src` into L2 ahead of use (16-byte aligned address, size a multiple of 16).
+// Hint: bring the L2 sector holding `src` (an in-bounds address) into L2.
+__device__ __forceinline__ void prefetch_l2(const void* src) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(src) : "memory");
+}
+
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }

@@ -4,7 +4,7 @@ Same buffers and attribute names as the reference's ``runtime/workspace.py:1-40`
 ``PlanBuffers`` holds the int32 SoA plan arrays and ``LayerBuffers`` the per-layer
 claim counter, fp32 partial/LSE split slots and the output.  Additions of the B200
 kernel: ``LayerBuffers.status`` (bounded-wait error word); ``counter`` has two words
-(claim counter + exit ticket).
+(claim counter + a spare word; the merge zeroes both).
 """
 from dataclasses import dataclass
 

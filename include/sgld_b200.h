@@ -151,7 +151,7 @@ typedef struct sgld_decode_args {
   int64_t vnew_stride[3];
   int32_t new_loc_int32;
   /* Layer scratch -- reference runtime/workspace.py:26-40 (LayerBuffers) */
-  int32_t* counter;     /* [2]  claim counter + exit ticket; zero before, left zero after    */
+  int32_t* counter;     /* [2]  claim counter + spare word; zero before, zeroed by the merge */
   float* partial;       /* [B, Hq, Smax, D] fp32 normalised split outputs, 16-byte aligned   */
   float* lse;           /* [B, Hq, Smax]    fp32 natural-log LSE per split                   */
   int32_t* status;      /* [1]  0 = ok; otherwise sticky error bits: 1-32 a bounded in-kernel
@@ -187,7 +187,7 @@ int sgld_merge_splits(const float* partial, const float* lse, const int32_t* cou
  * For callers that cannot allocate device memory: plugin interfaces that pass only input
  * and output buffers, or servers that give all device memory to their KV-cache pool at
  * start-up (cudaMalloc would also synchronise the device inside the serving loop).  The
- * decode's scratch (claim counter, exit ticket, fp32 partials and LSEs) lives in a 16 MiB
+ * decode's scratch (two claim words, fp32 partials and LSEs) lives in a 16 MiB
  * device array owned by the library on every GPU that loads it; args->counter, ->partial
  * and ->lse are ignored.  args->status must be a caller-owned device word (NULL is
  * rejected): bounded-wait and slot errors are reported there, as for

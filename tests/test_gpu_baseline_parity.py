@@ -48,7 +48,7 @@ def _run(b, cfg, data, mode):
     out = engine.execute(data["q"], data["k"], data["v"], data["pages"], indptr=data["indptr"])
     torch.cuda.synchronize()
     assert layer.status.item() == 0, "bounded in-kernel wait expired"
-    assert engine.counters.eq(0).all(), "claim counter / exit ticket not left at zero"
+    assert engine.counters.eq(0).all(), "claim words not left at zero"
     n = len(b.lengths)
     lb = b.lengths + [0] * (cfg.batch_capacity - n)
     sb = b.splits + [1] * (cfg.batch_capacity - n)

@@ -37,7 +37,7 @@ def run(engine, inputs, lengths, splits=None, indptr=None, layer=0, scale=None, 
                          k_scale=k_scale, v_scale=v_scale)
     torch.cuda.synchronize()
     assert lb.status.item() == 0, "bounded in-kernel wait expired"
-    assert engine.counters.eq(0).all(), "claim counter / exit ticket not left at zero"
+    assert engine.counters.eq(0).all(), "claim words not left at zero"
     return out
 
 
