@@ -537,6 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
     p.begin[i] = b;
     p.end[i] = e;
     p.weight[i] = w;
+    p.order[i] = i;                                  // R0/R1 order (the other modes rewrite it)
     s.weight[i] = w;
     vmax = max(vmax, w);
     vmin = min(vmin, w);
@@ -558,8 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1) plan_kernel(PlanLaunch a) {
   }
   if (tid == 0) *p.mode = mode;
 
-  if (mode == 0 || mode == 1) {
-    for (int i = tid; i < total; i += kThreads) p.order[i] = i;
+  if (mode == 0 || mode == 1) {                      // identity order, written during emission
     if (tid == 0) *p.num_packs = 0;
     return;
   }
