@@ -19,7 +19,8 @@ memory and a device->host copy of the output, on copy streams that overlap the
 neighbouring steps' compute), ``cpu_baseline`` (the FP32 CPU oracle on a bounded
 sample, scaled to one layer) and SM clocks sampled during the timed region.  Before
 timing, sampled requests are checked against a plain torch FP32 attention.  The steps are
-queued behind a short GPU spin and timed with one event pair (no event between launches, so
+queued behind a short GPU spin and PREROLL untimed steps (the first steps after a host
+synchronisation run slower than the steady state) and timed with one event pair (no event between launches, so
 the programmatic dependent launches stay chained); when the KV pool nearly fits in L2 (C1),
 L2 is flushed before every step and the steps are timed one by one instead.  The same step
 replayed from a CUDA graph is reported as ``config.graph_step_us``; small batches run the
@@ -47,6 +48,7 @@ for _p in (str(ROOT), str(ROOT / "-sglang-decode-_b200")):
 
 FALLBACK_HBM_GBS = 6650.0
 REF_ROUNDS = 3          # parallel CPU rounds per reference-arm step
+PREROLL = 5             # untimed steps between the start gate and the timed steps
 L2_BYTES = 126 * 2**20  # B200 L2
 METRIC = "paged GQA decode µs/layer + achieved HBM TB/s vs peak at 1/2/4/8 B200"
 
@@ -443,7 +445,16 @@ def run_ours(args):
             s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             # A ~1 ms spin ahead of the start event lets the host queue the first steps before
             # the GPU reaches them, so a short run does not time the host's first launches.
+            # PREROLL more untimed steps follow the spin.  After the host's synchronisation the
+            # first steps run slower than the steady state: step totals of the 8-way head shard
+            # of C3 at 2, 5, 20 and 80 steps fit 124.5 us a step plus about 30 us once.  A
+            # 20-step run would spread that over its steps.  Five steps bring it to the 80-step
+            # value; one does not.  The K timed steps are all full steps.
             torch.cuda._sleep(2_000_000)
+            for _ in range(PREROLL):
+                if before is not None:
+                    before()
+                body()
             s0.record(stream)
             for _ in range(n):
                 if before is not None:
@@ -636,6 +647,7 @@ def run_ours(args):
                               f"{kv_bytes >> 20} MB < 4 x 126 MB L2), steps timed one by one; e2e minus the "
                               f"measured write" if flush else
                               f"not flushed: KV pool per GPU {kv_bytes >> 20} MB > 4 x 126 MB L2"),
+                       "untimed_steps_before_timing": 0 if flush else PREROLL,
                        "kv_write": kv_write,
                        "self_check": "status 0, finite, sampled requests within 2e-2/2e-3 of FP32",
                        "decode_kernel": kind,
