@@ -8,8 +8,8 @@ Same API and checks as the reference's ``runtime/engine.py:1-74``:
 ``execute`` enqueues the sm_100a persistent decode kernel and the split merge (a
 programmatic dependent launch that overlaps the decode's tail) through the torch operator
 ``torch.ops.sglang_decode.decode``, which calls the C ABI; the claim counter is reset by
-the plan build and left at zero by the decode launch itself (the reference's per-layer
-memset is not needed).
+the plan build and left at zero by the call itself (the merge clears it once the decode has
+completed; the reference's per-layer memset is not needed).
 """
 from dataclasses import dataclass
 
