@@ -169,7 +169,9 @@ typedef struct sgld_decode_args {
  * pack claims); each task writes its normalised partial and LSE to slot
  * (request*Hq + head)*Smax + split; the merge combines each row's splits in split
  * order into `out`.  Rows with no record are written as zeros, or NaN when
- * plan->error is set.
+ * plan->error is set.  The merge launch leaves args->counter zero for the next call; a call
+ * that returns an error may leave it non-zero (zero it, or pass it to the next
+ * sgld_plan_build as a layer counter, before reusing it).
  */
 int sgld_decode_persistent(const sgld_decode_args* args, const sgld_plan_buffers* plan,
                            const sgld_plan_geometry* geometry, void* stream);
